@@ -1,0 +1,120 @@
+/*
+ * qwen3_b200.h -- C ABI of libqwen3_b200.so, the sm_100a (B200) decode kernels for Qwen3.
+ *
+ * The library is a drop-in for the kernels of William-Lamer/llm-inference. Its first ten
+ * entry points take exactly the parameters of the reference launchers in src/kernels.cuh:7-26
+ * (same order, same meaning, same units); each one's comment names the launcher it replaces.
+ * The differences are only those a C ABI needs:
+ *
+ *   - extern "C" linkage and an int status instead of void (Q3_OK = 0). Where the reference
+ *     prints a message and calls exit() (bad shapes, src/kernels.cu:147-152, :392-396; launch
+ *     errors, src/common.cuh:11-22) these return Q3_ERR_SHAPE or Q3_ERR_CUDA and change nothing.
+ *     csrc/dropin_shim.cu turns the codes back into the reference's print-and-exit behaviour
+ *     under the reference's C++ names, so the reference host code links unchanged.
+ *   - bf16 pointers are q3_bf16 (the 16 raw bits, layout-compatible with __nv_bfloat16).
+ *   - cudaStream_t is passed as void * (0 = the legacy default stream).
+ *
+ * Ownership and graph rules are the reference's (src/forward.cu:196-227): every pointer is
+ * caller-owned device memory, launchers allocate nothing and never synchronize, positions and
+ * token ids are read from device memory inside the kernels, so a launch sequence captured in
+ * a CUDA graph stays valid for every position. All kernels are launched with programmatic
+ * stream serialization: each may start while the previous kernel on the stream finishes,
+ * prefetching weights, and waits for it before touching activations.
+ *
+ * Preconditions, as in the reference: matrix column counts are multiples of 8 and matrix,
+ * vector and cache pointers are 16-byte aligned (the reference's uint4 loads need the same,
+ * src/kernels.cu:146-152); head_dim is a multiple of 32 up to 1024; n_heads is a multiple of
+ * n_kv_heads.
+ */
+#ifndef QWEN3_B200_H
+#define QWEN3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef uint16_t q3_bf16;
+
+enum q3_status {
+    Q3_OK = 0,
+    Q3_ERR_SHAPE = 1,    /* a size violates a precondition (the reference would exit) */
+    Q3_ERR_ALIGN = 2,    /* a pointer is not 16-byte aligned */
+    Q3_ERR_CUDA = 3,     /* a CUDA call failed; q3_last_cuda_error() gives the cudaError_t */
+    Q3_ERR_DEVICE = 4,   /* the current device is not sm_100 (B200) */
+    Q3_ERR_ARG = 5,      /* a null pointer or an invalid option */
+};
+
+/* Text for a q3_status value. */
+const char *q3_status_string(int status);
+
+/* The cudaError_t behind the most recent Q3_ERR_CUDA on this thread. */
+int q3_last_cuda_error(void);
+
+/* Reads and clears the device error flags that bounded waits and range checks inside the
+ * kernels set (bit 0: a wait timed out, bit 1: token id out of range, bit 2: position out of
+ * range). Synchronizes `stream` first. Returns a q3_status; the flags go to *flags. */
+int q3_device_error(void *stream, unsigned *flags);
+
+/* ---------------------------------------------------------------------------------------
+ * Drop-in launchers (batch 1). Each replaces the launcher of the same name without the
+ * q3_ prefix in src/kernels.cuh, with identical parameters.
+ * ------------------------------------------------------------------------------------- */
+
+/* src/kernels.cuh:7-8 embedding_forward: out[i] = table[*d_token * hidden + i]. */
+int q3_embedding_forward(q3_bf16 *out, const q3_bf16 *table, const int *d_token, int hidden,
+                         void *stream);
+
+/* src/kernels.cuh:9-10 rmsnorm_forward: per row y = bf16(bf16(x * rsqrt(mean(x^2) + eps)) * w). */
+int q3_rmsnorm_forward(q3_bf16 *out, const q3_bf16 *in, const q3_bf16 *weight, int rows, int dim,
+                       float eps, void *stream);
+
+/* src/kernels.cuh:11 gemv_forward: out[r] = bf16(w[r] . x), w is [rows, cols] row-major. */
+int q3_gemv_forward(q3_bf16 *out, const q3_bf16 *w, const q3_bf16 *x, int rows, int cols,
+                    void *stream);
+
+/* src/kernels.cuh:12-13 gemv_residual_forward: y = bf16(w[r] . in); tap[r] = y if tap;
+ * x[r] = bf16(x[r] + y). */
+int q3_gemv_residual_forward(q3_bf16 *x, const q3_bf16 *w, const q3_bf16 *in, int rows, int cols,
+                             q3_bf16 *tap, void *stream);
+
+/* src/kernels.cuh:14-15 qkv_forward: q = wq . x, k = wk . x, v = wv . x. */
+int q3_qkv_forward(q3_bf16 *q, q3_bf16 *k, q3_bf16 *v, const q3_bf16 *wq, const q3_bf16 *wk,
+                   const q3_bf16 *wv, const q3_bf16 *x, int q_rows, int kv_rows, int cols,
+                   void *stream);
+
+/* src/kernels.cuh:16-17 gate_up_forward: act[r] = bf16(bf16(silu(g)) * u) with
+ * g = bf16(w_gate[r] . x), u = bf16(w_up[r] . x); gate_tap/up_tap receive g and u if non-null. */
+int q3_gate_up_forward(q3_bf16 *act, const q3_bf16 *w_gate, const q3_bf16 *w_up,
+                       const q3_bf16 *x, int rows, int cols, q3_bf16 *gate_tap, q3_bf16 *up_tap,
+                       void *stream);
+
+/* src/kernels.cuh:18-21 qk_norm_rope_forward: per-head RMSNorm of q and k, neox RoPE at
+ * position *d_pos, in place; k and v are written to key_cache/value_cache row *d_pos (one
+ * layer's [max_seq, n_kv_heads * head_dim] caches). q_tap/k_tap receive the normed heads. */
+int q3_qk_norm_rope_forward(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_bf16 *q_norm_w,
+                            const q3_bf16 *k_norm_w, q3_bf16 *key_cache, q3_bf16 *value_cache,
+                            const int *d_pos, int n_heads, int n_kv_heads, int head_dim, float eps,
+                            float theta, q3_bf16 *q_tap, q3_bf16 *k_tap, void *stream);
+
+/* src/kernels.cuh:22-24 attention_forward: GQA decode attention of q over cache positions
+ * 0..*d_pos with the reference's rounding points; att is caller scratch [n_heads, max_seq]. */
+int q3_attention_forward(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache,
+                         const q3_bf16 *value_cache, float *att, int n_heads, int n_kv_heads,
+                         int head_dim, const int *d_pos, int max_seq, float scale, void *stream);
+
+/* src/kernels.cuh:25 argmax_forward: *out = index of the largest of x[0..n), lowest index on
+ * ties, NaN never chosen. */
+int q3_argmax_forward(int *out, const q3_bf16 *x, int n, void *stream);
+
+/* src/kernels.cuh:26 sample_forward: inverse-CDF sample from softmax(x * inv_temp) with the
+ * host uniform u in [0, 1); *out = -1 if no token is found. */
+int q3_sample_forward(int *out, const q3_bf16 *x, int n, float inv_temp, float u, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QWEN3_B200_H */

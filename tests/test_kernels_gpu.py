@@ -1,0 +1,129 @@
+"""Parity of the drop-in launchers (batch 1) on a B200, through the C ABI.
+
+Every case of tests/golden/cases.py runs through libqwen3_b200.so and is compared with
+  - the reference's own kernels: bit for bit (0 ulp). The fixture ref_kernels.npz holds their
+    outputs; where oracle/_ref/libqwen3_ref.so was shipped the test also runs them live;
+  - the CPU oracle, within the per-kind tolerance of test_oracle_golden.ORACLE_TOL (the
+    oracle's libm differs from CUDA's in the last bit).
+"""
+import ctypes
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE / "golden"))
+import cases  # noqa: E402
+import oracle as O  # noqa: E402
+from test_oracle_golden import GOLDEN, ORACLE_TOL  # noqa: E402
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+def _reference_outputs(kind, name, p, inp):
+    if GOLDEN.exists():
+        g = np.load(GOLDEN)
+        if f"{name}/digest" in g.files:
+            assert str(g[f"{name}/digest"]) == cases.input_digest(inp)
+            return {k.split("/", 1)[1]: g[k] for k in g.files if k.startswith(name + "/") and not k.endswith("/digest")}
+    import ref_kernels
+    if ref_kernels.available():
+        return cases.run("ref", kind, p, inp)
+    pytest.skip("no reference outputs: neither the fixture nor oracle/_ref is present")
+
+
+@pytest.mark.parametrize("kind,name,p", cases.CASES, ids=[c[1] for c in cases.CASES])
+def test_dropin_kernel_bit_exact(kind, name, p):
+    inp = cases.inputs(kind, p)
+    mine = cases.run("mine", kind, p, inp)
+    ref = _reference_outputs(kind, name, p, inp)
+    for k, v in mine.items():
+        assert v.shape == ref[k].shape, k
+        if v.dtype == np.uint16:
+            d = O.ulp_diff(v, ref[k])
+            assert d.max() == 0, f"{k}: {np.count_nonzero(d)} elements differ, max {d.max()} ulp"
+        else:
+            assert np.array_equal(v, ref[k]), f"{k}: {v} vs {ref[k]}"
+
+
+@pytest.mark.parametrize("kind,name,p", cases.CASES, ids=[c[1] for c in cases.CASES])
+def test_dropin_kernel_vs_oracle(kind, name, p):
+    inp = cases.inputs(kind, p)
+    mine = cases.run("mine", kind, p, inp)
+    orc = cases.run("oracle", kind, p, inp)
+    max_ulp, max_frac = ORACLE_TOL[kind]
+    for k, v in mine.items():
+        if v.dtype == np.uint16:
+            d = O.ulp_diff(v, orc[k])
+            assert d.max() <= max_ulp and np.mean(d > 0) <= max_frac, f"{k}: max {d.max()} ulp"
+        else:
+            assert np.array_equal(v, orc[k]), f"{k}: {v} vs {orc[k]}"
+
+
+def _pkg():
+    sys.path.insert(0, str(HERE))
+    import conftest  # noqa: F401
+    import llm_inference_b200 as q3
+    return q3
+
+
+def test_shape_errors_are_reported_not_fatal():
+    q3 = _pkg()
+    w = torch.zeros(16, 12, dtype=torch.bfloat16, device="cuda")
+    x = torch.zeros(12, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(16, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(q3.Q3Error) as e:
+        q3.gemv_forward(out, w, x, 16, 12)  # cols % 8 != 0 (the reference exits here)
+    assert e.value.status == 1
+    q = torch.zeros(48, dtype=torch.bfloat16, device="cuda")
+    pos = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(q3.Q3Error):
+        q3.qk_norm_rope_forward(q, q, q, q, q, q, q, pos, 1, 1, 48, 1e-6, 1e6)  # head_dim % 32
+    with pytest.raises(q3.Q3Error) as e:
+        q3.gemv_forward(out, w[:, 1:], x, 16, 8)  # misaligned weight pointer
+    assert e.value.status == 2
+    assert q3.device_error() == 0
+
+
+def test_launch_sequence_captures_in_a_cuda_graph():
+    """The reference replays one captured graph per token (src/forward.cu:196-227); the
+    launchers must be capturable, including their first call, and read pos from memory."""
+    q3 = _pkg()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    H, V = 256, 512
+    table = torch.randn(V, H, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(H, H, generator=g, device="cuda") * 0.02).bfloat16()
+    tok = torch.tensor([3], dtype=torch.int32, device="cuda")
+    x = torch.empty(H, dtype=torch.bfloat16, device="cuda")
+    xb = torch.empty_like(x)
+    nw = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    logits = torch.empty(V, dtype=torch.bfloat16, device="cuda")
+    best = torch.empty(1, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        s = torch.cuda.current_stream().cuda_stream
+        q3.embedding_forward(x, table, tok, H, stream=s)
+        q3.rmsnorm_forward(xb, x, nw, 1, H, 1e-6, stream=s)
+        q3.gemv_residual_forward(x, w, xb, H, H, stream=s)
+        q3.gemv_forward(logits, table, x, V, H, stream=s)
+        q3.argmax_forward(best, logits, V, stream=s)
+    for token in (3, 100, 511):
+        tok.fill_(token)
+        graph.replay()
+        torch.cuda.synchronize()
+        # the same launches run eagerly give the same logits and token
+        xr = torch.empty_like(x)
+        q3.embedding_forward(xr, table, tok, H)
+        q3.rmsnorm_forward(xb, xr, nw, 1, H, 1e-6)
+        q3.gemv_residual_forward(xr, w, xb, H, H)
+        lg = torch.empty_like(logits)
+        q3.gemv_forward(lg, table, xr, V, H)
+        b2 = torch.empty_like(best)
+        q3.argmax_forward(b2, lg, V)
+        torch.cuda.synchronize()
+        assert torch.equal(lg, logits) and int(b2) == int(best)
+    assert q3.device_error() == 0
