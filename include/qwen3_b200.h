@@ -113,6 +113,144 @@ int q3_argmax_forward(int *out, const q3_bf16 *x, int n, void *stream);
  * host uniform u in [0, 1); *out = -1 if no token is found. */
 int q3_sample_forward(int *out, const q3_bf16 *x, int n, float inv_temp, float u, void *stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Batched launchers: `batch` independent decode sequences. The reference has no batch
+ * dimension; per sequence each computes what the reference launcher computes for it.
+ * Activations are [batch, dim] row-major. Sequence b's KV cache rows start at
+ * cache + b * cache_seq_stride (elements); token ids and positions are per sequence in
+ * device memory. Projections with batch 1 run the bit-exact batch-1 kernels; batch >= 2 runs
+ * the tcgen05 tensor-core GEMM (fp32 sums in the tensor core's order).
+ * ------------------------------------------------------------------------------------- */
+
+/* out[b] = table[d_tokens[b]]; an id outside [0, vocab) writes zeros and sets device error
+ * bit 1 instead of reading outside the table. */
+int q3_embedding_batched(q3_bf16 *out, const q3_bf16 *table, const int *d_tokens, int batch, int hidden,
+                         int vocab, void *stream);
+
+/* out[b][r] = bf16(w[r] . x[b]) */
+int q3_gemv_batched(q3_bf16 *out, const q3_bf16 *w, const q3_bf16 *x, int batch, int rows, int cols,
+                    void *stream);
+
+/* x[b][r] = bf16(x[b][r] + bf16(w[r] . in[b])) */
+int q3_gemv_residual_batched(q3_bf16 *x, const q3_bf16 *w, const q3_bf16 *in, int batch, int rows, int cols,
+                             q3_bf16 *tap, void *stream);
+
+int q3_qkv_batched(q3_bf16 *q, q3_bf16 *k, q3_bf16 *v, const q3_bf16 *wq, const q3_bf16 *wk, const q3_bf16 *wv,
+                   const q3_bf16 *x, int batch, int q_rows, int kv_rows, int cols, void *stream);
+
+int q3_gate_up_batched(q3_bf16 *act, const q3_bf16 *w_gate, const q3_bf16 *w_up, const q3_bf16 *x, int batch,
+                       int rows, int cols, q3_bf16 *gate_tap, q3_bf16 *up_tap, void *stream);
+
+/* qk_norm_rope_forward per sequence at position d_pos[b]; positions outside [0, max_seq) set
+ * device error bit 2 and skip that sequence. */
+int q3_qk_norm_rope_batched(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_bf16 *q_norm_w,
+                            const q3_bf16 *k_norm_w, q3_bf16 *key_cache, q3_bf16 *value_cache,
+                            long long cache_seq_stride, const int *d_pos, int batch, int n_heads, int n_kv_heads,
+                            int head_dim, int max_seq, float eps, float theta, q3_bf16 *q_tap, q3_bf16 *k_tap,
+                            void *stream);
+
+/* Bytes of scratch q3_attention_batched needs (0 for unsupported shapes: head_dim above 256 or
+ * a group size n_heads / n_kv_heads other than 1, 2, 4 or 8). */
+size_t q3_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
+
+/* Split-KV attention per sequence over positions 0..d_pos[b]. `scratch` (size from
+ * q3_attention_scratch_bytes) must be zeroed once before the first call; calls leave it ready
+ * for the next one. Calls sharing a scratch buffer must not overlap on the GPU. */
+int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache, const q3_bf16 *value_cache,
+                         long long cache_seq_stride, void *scratch, const int *d_pos, int batch, int n_heads,
+                         int n_kv_heads, int head_dim, int max_seq, float scale, void *stream);
+
+/* out[b] = argmax of x[b][0..n) with argmax_forward's tie and NaN rules. */
+int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream);
+
+/* dst[i] = bf16(mean + std * N(0,1)), a counter-based generator seeded by `seed` (synthetic
+ * weights and KV caches for benchmarks). */
+int q3_fill_normal_bf16(q3_bf16 *dst, long long n, unsigned long long seed, float mean, float std, void *stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Decode engine: the reference's forward pass (src/forward.cu:118-236) for `batch`
+ * sequences with all state on the device and one CUDA graph per decode step.
+ * ------------------------------------------------------------------------------------- */
+
+/* The model shape, as src/model.cuh:10-24 (Config) reads it from config.json. */
+typedef struct q3_config {
+    int hidden_size;
+    int intermediate_size;
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int head_dim;
+    int vocab_size;
+    float rms_norm_eps;
+    float rope_theta;
+} q3_config;
+
+/* Device pointers of one layer, fields as src/model.cuh:26-39 (LayerWeights); matrices are
+ * [out, in] row-major. */
+typedef struct q3_layer_weights {
+    const q3_bf16 *attn_norm, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *mlp_norm, *w_gate, *w_up, *w_down;
+} q3_layer_weights;
+
+/* src/model.cuh:47-59 (Weights): `layers` is a host array of n_layers entries; lm_head equals
+ * embed for tied embeddings. The engine keeps the pointers, not copies of the weights. */
+typedef struct q3_weights {
+    const q3_bf16 *embed;
+    const q3_layer_weights *layers;
+    const q3_bf16 *final_norm;
+    const q3_bf16 *lm_head;
+} q3_weights;
+
+typedef struct q3_engine q3_engine;
+
+/* Device buffers of an engine, for inspection. */
+typedef struct q3_engine_buffers {
+    q3_bf16 *x;            /* [batch, hidden] residual stream after the last step */
+    q3_bf16 *logits;       /* [batch, vocab] */
+    q3_bf16 *key_cache;    /* [n_layers][batch][max_seq][n_kv_heads * head_dim] */
+    q3_bf16 *value_cache;
+    int *next_token;       /* [batch] read by the next step's embedding */
+    int *pos;              /* [batch] position the next step writes and attends up to */
+    int *out_token;        /* [batch] argmax of the last step */
+    int *history;          /* [history_cap][batch] tokens of steps 0, 1, ... */
+    int *step;             /* steps run since creation */
+    int batch, max_seq, history_cap;
+    int launches_per_step; /* kernel launches in the captured step (0 before q3_engine_capture) */
+} q3_engine_buffers;
+
+enum { Q3_ENGINE_EXACT_ATTENTION = 1 /* bit-exact single-chunk attention instead of split-KV */ };
+
+/* src/forward.cu:83-114 weight_bytes_per_step and kv_bytes_per_position. */
+size_t q3_weight_bytes_per_step(const q3_config *cfg);
+size_t q3_kv_bytes_per_position(const q3_config *cfg);
+
+/* Allocates the run state for `batch` sequences of up to `max_seq` positions (caches zeroed,
+ * tokens and positions 0) on the current device; work goes to `stream`, or to a stream the
+ * engine creates when `stream` is 0 (the legacy default stream cannot be captured). */
+int q3_engine_create(const q3_config *cfg, const q3_weights *weights, int batch, int max_seq, int history_cap,
+                     int flags, void *stream, q3_engine **out);
+int q3_engine_destroy(q3_engine *e);
+
+/* Captures one decode step into a CUDA graph (src/forward.cu:196-204); q3_engine_step then
+ * replays it. Without a capture, steps launch their kernels one by one. */
+int q3_engine_capture(q3_engine *e);
+
+/* Runs n decode steps back to back on the device: each embeds next_token[b], runs the layers at
+ * pos[b], and its argmax writes next_token[b], out_token[b] and history, then advances pos[b]. */
+int q3_engine_step(q3_engine *e, int n_steps);
+
+/* Copies host token ids and positions ([batch] each) to the device (src/forward.cu:218-220). */
+int q3_engine_set_state(q3_engine *e, const int *tokens, const int *positions);
+
+/* The reference's per-token protocol: forward = set_state + one step (src/forward.cu:206-227);
+ * sample_argmax copies the step's tokens to the host and waits for them (:229-236). */
+int q3_engine_forward(q3_engine *e, const int *tokens, const int *positions);
+int q3_engine_sample_argmax(q3_engine *e, int *tokens_out);
+
+/* Fills cache positions [0, n_positions) of every layer and sequence with bf16 N(0,1). */
+int q3_engine_fill_kv_normal(q3_engine *e, int n_positions, unsigned long long seed);
+
+int q3_engine_info(const q3_engine *e, q3_engine_buffers *out);
+
 #ifdef __cplusplus
 }
 #endif

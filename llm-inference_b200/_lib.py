@@ -39,8 +39,30 @@ SIGNATURES: dict[str, list] = {
     "q3_attention_forward": [_P, _P, _P, _P, _P, _I, _I, _I, _P, _I, _F, _P],
     "q3_argmax_forward": [_P, _P, _I, _P],
     "q3_sample_forward": [_P, _P, _I, _F, _F, _P],
+    "q3_embedding_batched": [_P, _P, _P, _I, _I, _I, _P],
+    "q3_gemv_batched": [_P, _P, _P, _I, _I, _I, _P],
+    "q3_gemv_residual_batched": [_P, _P, _P, _I, _I, _I, _P, _P],
+    "q3_qkv_batched": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
+    "q3_gate_up_batched": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
+    "q3_qk_norm_rope_batched": [_P, _P, _P, _P, _P, _P, _P, _LL, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P],
+    "q3_attention_scratch_bytes": [_I, _I, _I, _I, _I],
+    "q3_attention_batched": [_P, _P, _P, _P, _LL, _P, _P, _I, _I, _I, _I, _I, _F, _P],
+    "q3_argmax_batched": [_P, _P, _I, _I, _P],
+    "q3_fill_normal_bf16": [_P, _LL, ctypes.c_ulonglong, _F, _F, _P],
+    "q3_weight_bytes_per_step": [_P],
+    "q3_kv_bytes_per_position": [_P],
+    "q3_engine_create": [_P, _P, _I, _I, _I, _I, _P, _P],
+    "q3_engine_destroy": [_P],
+    "q3_engine_capture": [_P],
+    "q3_engine_step": [_P, _I],
+    "q3_engine_set_state": [_P, _P, _P],
+    "q3_engine_forward": [_P, _P, _P],
+    "q3_engine_sample_argmax": [_P, _P],
+    "q3_engine_fill_kv_normal": [_P, _I, ctypes.c_ulonglong],
+    "q3_engine_info": [_P, _P],
 }
-RESTYPES = {"q3_status_string": ctypes.c_char_p}
+RESTYPES = {"q3_status_string": ctypes.c_char_p, "q3_attention_scratch_bytes": ctypes.c_size_t,
+            "q3_weight_bytes_per_step": ctypes.c_size_t, "q3_kv_bytes_per_position": ctypes.c_size_t}
 
 _lib = None
 

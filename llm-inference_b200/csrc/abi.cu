@@ -23,9 +23,8 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
                  long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
-                int *pos, int *history, int *step, cudaStream_t s);
+                int *pos, int *history, int *step, int history_cap, cudaStream_t s);
 int sample(int *out, const bf16 *x, int n, float inv_temp, float u, cudaStream_t s);
-struct AttnSplit;
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
               const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
               int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
@@ -33,6 +32,7 @@ int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value
 unsigned take_error_gemv();
 unsigned take_error_decode();
 unsigned take_error_attention();
+unsigned take_error_tc();
 
 namespace {
 constexpr int MAX_DEVICES = 64;
@@ -134,7 +134,7 @@ int q3_device_error(void *stream, unsigned *flags) {
     if (!flags) return Q3_ERR_ARG;
     cudaError_t e = cudaStreamSynchronize(S(stream));
     if (e != cudaSuccess) return q3::record_cuda_error(e);
-    *flags = q3::take_error_gemv() | q3::take_error_decode() | q3::take_error_attention();
+    *flags = q3::take_error_gemv() | q3::take_error_decode() | q3::take_error_attention() | q3::take_error_tc();
     return Q3_OK;
 }
 
@@ -195,7 +195,7 @@ int q3_attention_forward(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
 
 int q3_argmax_forward(int *out, const q3_bf16 *x, int n, void *stream) {
     DEVICE_OR_RETURN();
-    return q3::argmax_rows(CB(x), n, 1, 0, out, nullptr, nullptr, nullptr, nullptr, S(stream));
+    return q3::argmax_rows(CB(x), n, 1, 0, out, nullptr, nullptr, nullptr, nullptr, 0, S(stream));
 }
 
 int q3_sample_forward(int *out, const q3_bf16 *x, int n, float inv_temp, float u, void *stream) {

@@ -445,12 +445,6 @@ int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int 
 
 // Attention over n_rows sequences. Exact mode when split == nullptr; otherwise `split` holds the
 // split-mode scratch (stats, partial, count_a, count_b, chunk_b, max_chunks).
-struct AttnSplit {
-    float *stats;
-    float *partial;
-    int *count_a, *count_b;
-    int chunk_b, max_chunks;
-};
 
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
               const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,

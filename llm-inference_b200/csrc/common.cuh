@@ -187,6 +187,16 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Scratch of the split-KV attention (attention.cu): softmax statistics, per-chunk partial
+// outputs and two per-(sequence, kv head) counters that must be zero before the first call
+// (the kernels return them to zero).
+struct AttnSplit {
+    float *stats;
+    float *partial;
+    int *count_a, *count_b;
+    int chunk_b, max_chunks;
+};
+
 int num_sms();               // SM count of the current device (cached per device)
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the current device (cached, so
 // repeated launches make no runtime call; safe during stream capture).

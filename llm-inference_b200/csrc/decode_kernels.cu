@@ -186,8 +186,9 @@ struct ArgmaxOut {
     int *out;          // out[b]
     int *next_token;   // optional: next_token[b] = out[b] (decode loop)
     int *pos;          // optional: pos[b] += 1 (decode loop)
-    int *history;      // optional: history[*step * n_rows + b] = token (decode loop)
+    int *history;      // optional: history[*step * n_rows + b] = token while *step < history_cap
     int *step;         // optional: step counter, incremented once per launch
+    int history_cap;   // rows of `history`
 };
 
 template <bool VEC>
@@ -249,7 +250,8 @@ __global__ void __launch_bounds__(ARGMAX_THREADS) argmax_kernel(const bf16 *x, i
         }
         o.out[row] = best_idx;
         if (o.next_token) o.next_token[row] = best_idx;
-        if (o.history) o.history[(size_t)(*o.step) * (gridDim.x / ARGMAX_CTAS) + row] = best_idx;
+        if (o.history && *o.step >= 0 && *o.step < o.history_cap)
+            o.history[(size_t)(*o.step) * (gridDim.x / ARGMAX_CTAS) + row] = best_idx;
         if (o.pos) o.pos[row] += 1;
     }
     cluster.sync();  // keep every CTA's shared memory alive until rank 0 has read it
@@ -309,7 +311,37 @@ __global__ void __launch_bounds__(1024) sample_kernel(int *out, const bf16 *x, i
     *out = chosen;
 }
 
+// ------------------------------------------------------------------ synthetic fill
+// dst[i] = bf16(mean + std * z), z ~ N(0, 1) from a counter-based hash of (seed, i) and the
+// Box-Muller transform; used to pre-fill KV caches and weights of synthetic benchmarks.
+__device__ __forceinline__ uint32_t mix32(uint64_t x) {
+    x ^= x >> 33;
+    x *= 0xff51afd7ed558ccdull;
+    x ^= x >> 33;
+    x *= 0xc4ceb9fe1a85ec53ull;
+    x ^= x >> 33;
+    return (uint32_t)x;
+}
+
+__global__ void fill_normal_kernel(bf16 *dst, long long n, unsigned long long seed, float mean, float std) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const uint64_t c = seed * 0x9e3779b97f4a7c15ull + (uint64_t)i;
+        const float u1 = ((mix32(2 * c) >> 8) + 1) * (1.0f / 16777217.0f);  // (0, 1]
+        const float u2 = (mix32(2 * c + 1) >> 8) * (1.0f / 16777216.0f);
+        const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+        dst[i] = __float2bfloat16(mean + std * z);
+    }
+}
+
 }  // namespace
+
+int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s) {
+    if (!dst || n < 0) return Q3_ERR_ARG;
+    if (n == 0) return Q3_OK;
+    const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
+    fill_normal_kernel<<<blocks, 256, 0, s>>>(dst, n, seed, mean, std);
+    return record_cuda_error(cudaGetLastError());
+}
 
 unsigned take_error_decode() {
     unsigned v = 0, zero = 0;
@@ -374,10 +406,11 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
 }
 
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
-                int *pos, int *history, int *step, cudaStream_t s) {
+                int *pos, int *history, int *step, int history_cap, cudaStream_t s) {
     if (!x || !out) return Q3_ERR_ARG;
     if (n < 0 || n_rows <= 0) return n_rows == 0 ? Q3_OK : Q3_ERR_SHAPE;
-    ArgmaxOut o = {out, next_token, pos, history, step};
+    if (history && !step) return Q3_ERR_ARG;
+    ArgmaxOut o = {out, next_token, pos, history, step, history_cap};
     const bool vec = aligned16(x) && (row_stride % 8 == 0 || n_rows == 1);
     dim3 grid(ARGMAX_CTAS * n_rows);
     if (vec) Q3_TRY_LAUNCH(launch(argmax_kernel<true>, grid, dim3(ARGMAX_THREADS), 0, s, ARGMAX_CTAS, x, n, row_stride, o));

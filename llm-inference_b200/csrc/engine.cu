@@ -1,0 +1,350 @@
+// Batched greedy decode engine: the reference's forward pass (src/forward.cu) for B independent
+// sequences on one GPU, with every buffer on the device and one CUDA graph per decode step.
+//
+// RunState (src/forward.cuh:6-25) becomes batched: activations [B, dim], one KV cache per layer
+// and sequence ([n_layers][B][max_seq][kv_dim], sequence b of layer l at
+// key_cache + (l*B + b)*max_seq*kv_dim), per-sequence token ids and positions in device memory.
+// The launch order of one step is forward_kernels (src/forward.cu:118-193) followed by the
+// greedy argmax (:229-236), which here also feeds the next step on the device: it writes
+// next_token[b], advances pos[b] and appends the token to a history buffer, so a captured step
+// replays back to back with no host round trip. The reference protocol -- host token and
+// position in, one step, host token out -- is q3_engine_forward + q3_engine_sample_argmax.
+//
+// Projections: batch 1 uses the bit-exact batch-1 kernels, batch >= 2 the tcgen05 GEMM.
+// Attention: split-KV by default; Q3_ENGINE_EXACT_ATTENTION selects the bit-exact single-chunk
+// kernels (slower at long context).
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "common.cuh"
+
+namespace q3 {
+int check_device();
+int proj(bf16 *out, const bf16 *w, const bf16 *x, int batch, int rows, int cols, cudaStream_t s);
+int proj_residual(bf16 *x, const bf16 *w, const bf16 *in, int batch, int rows, int cols, bf16 *tap,
+                  cudaStream_t s);
+int proj_qkv(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf16 *wv, const bf16 *x,
+             int batch, int q_rows, int kv_rows, int cols, cudaStream_t s);
+int proj_gate_up(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int batch, int rows, int cols,
+                 bf16 *gate_tap, bf16 *up_tap, cudaStream_t s);
+int embedding(bf16 *out, const bf16 *table, const int *tokens, int n_rows, int hidden, int vocab,
+              cudaStream_t s);
+int rmsnorm(bf16 *out, const bf16 *in, const bf16 *weight, int rows, int dim, float eps, cudaStream_t s);
+int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf16 *k_norm_w,
+                 bf16 *key_cache, bf16 *value_cache, const int *pos, int n_rows, long long q_stride,
+                 long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
+                 int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
+int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
+                int *pos, int *history, int *step, int history_cap, cudaStream_t s);
+int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
+              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
+              int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
+              cudaStream_t s);
+int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
+size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, AttnSplit *sp,
+                                float **scores, void *base);
+int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s);
+}  // namespace q3
+
+using namespace q3;
+
+struct q3_engine {
+    q3_config cfg;
+    std::vector<q3_layer_weights> layers;
+    const bf16 *embed, *final_norm, *lm_head;
+    int B, max_seq, history_cap, flags;
+    cudaStream_t stream;
+    // activations
+    bf16 *x, *xb, *q, *k, *v, *attn_out, *hb, *logits;
+    bf16 *key_cache, *value_cache;
+    void *attn_scratch;
+    float *scores;
+    AttnSplit split;
+    // decode-loop state
+    int *next_token, *pos, *out_token, *history, *step;
+    int *host_io;  // pinned: [2B] for token/position uploads, [B] for downloads
+    cudaGraphExec_t graph;
+    int graph_kernels;  // kernel nodes of the captured step
+    cudaStream_t own_stream;  // created when the caller passes the legacy default stream
+    std::vector<void *> allocations;
+};
+
+namespace {
+
+int alloc(q3_engine *e, void **p, size_t bytes) {
+    cudaError_t err = cudaMalloc(p, bytes);
+    if (err != cudaSuccess) return record_cuda_error(err);
+    e->allocations.push_back(*p);
+    return Q3_OK;
+}
+
+#define TRY(expr)                     \
+    do {                              \
+        int st_ = (expr);             \
+        if (st_ != Q3_OK) return st_; \
+    } while (0)
+
+int enqueue_step(q3_engine *e) {
+    const q3_config &c = e->cfg;
+    const int B = e->B, H = c.hidden_size, I = c.intermediate_size;
+    const int qd = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
+    const long long seq_stride = (long long)e->max_seq * kvd;
+    const float scale = (float)(1.0 / sqrt((double)c.head_dim));
+    cudaStream_t s = e->stream;
+    const bool exact_attn = (e->flags & Q3_ENGINE_EXACT_ATTENTION) != 0;
+
+    TRY(embedding(e->x, e->embed, e->next_token, B, H, c.vocab_size, s));
+    for (int l = 0; l < c.n_layers; l++) {
+        const q3_layer_weights &w = e->layers[l];
+        bf16 *kc = e->key_cache + (size_t)l * B * seq_stride;
+        bf16 *vc = e->value_cache + (size_t)l * B * seq_stride;
+        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.attn_norm, B, H, c.rms_norm_eps, s));
+        TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, B, qd, kvd,
+                     H, s));
+        TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, e->pos, B, qd,
+                         kvd, seq_stride, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps,
+                         c.rope_theta, nullptr, nullptr, s));
+        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, e->pos, B, qd, seq_stride, c.n_heads, c.n_kv_heads,
+                      c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
+        TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, B, H, qd, nullptr, s));
+        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, B, H, c.rms_norm_eps, s));
+        TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, B, I, H, nullptr, nullptr, s));
+        TRY(proj_residual(e->x, (const bf16 *)w.w_down, e->hb, B, H, I, nullptr, s));
+    }
+    TRY(rmsnorm(e->xb, e->x, e->final_norm, B, H, c.rms_norm_eps, s));
+    TRY(proj(e->logits, e->lm_head, e->xb, B, c.vocab_size, H, s));
+    TRY(argmax_rows(e->logits, c.vocab_size, B, c.vocab_size, e->out_token, e->next_token, e->pos, e->history,
+                    e->step, e->history_cap, s));
+    return Q3_OK;
+}
+
+void release(q3_engine *e) {
+    if (e->graph) cudaGraphExecDestroy(e->graph);
+    if (e->own_stream) cudaStreamDestroy(e->own_stream);
+    for (void *p : e->allocations) cudaFree(p);
+    if (e->host_io) cudaFreeHost(e->host_io);
+    delete e;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t q3_weight_bytes_per_step(const q3_config *c) {
+    if (!c) return 0;
+    const size_t hidden = c->hidden_size, hd = c->head_dim, q = (size_t)c->n_heads * hd,
+                 kv = (size_t)c->n_kv_heads * hd, inter = c->intermediate_size;
+    size_t layer = hidden + q * hidden + 2 * kv * hidden + 2 * hd + hidden * q + hidden + 3 * inter * hidden;
+    size_t elems = layer * c->n_layers + hidden + (size_t)c->vocab_size * hidden + hidden;
+    return elems * 2;
+}
+
+size_t q3_kv_bytes_per_position(const q3_config *c) {
+    if (!c) return 0;
+    return 2 * (size_t)c->n_layers * c->n_kv_heads * c->head_dim * 2;
+}
+
+int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int max_seq, int history_cap, int flags,
+                     void *stream, q3_engine **out) {
+    if (!cfg || !w || !out || !w->layers || !w->embed || !w->final_norm || !w->lm_head) return Q3_ERR_ARG;
+    *out = nullptr;
+    int st = check_device();
+    if (st != Q3_OK) return st;
+    const q3_config &c = *cfg;
+    if (batch <= 0 || max_seq <= 0 || history_cap < 0 || c.n_layers <= 0 || c.hidden_size <= 0 ||
+        c.intermediate_size <= 0 || c.vocab_size <= 0 || c.hidden_size % 8 || c.intermediate_size % 8)
+        return Q3_ERR_SHAPE;
+    st = attention_check(c.n_heads, c.n_kv_heads, c.head_dim, max_seq, batch);
+    if (st != Q3_OK) return st;
+    q3_engine *e = new q3_engine();
+    e->cfg = c;
+    e->layers.assign(w->layers, w->layers + c.n_layers);
+    e->embed = (const bf16 *)w->embed;
+    e->final_norm = (const bf16 *)w->final_norm;
+    e->lm_head = (const bf16 *)w->lm_head;
+    e->B = batch;
+    e->max_seq = max_seq;
+    e->history_cap = history_cap;
+    e->flags = flags;
+    e->stream = (cudaStream_t)stream;
+    if (e->stream == nullptr) {  // stream capture is not possible on the legacy default stream
+        cudaError_t err = cudaStreamCreateWithFlags(&e->own_stream, cudaStreamNonBlocking);
+        if (err != cudaSuccess) {
+            release(e);
+            return record_cuda_error(err);
+        }
+        e->stream = e->own_stream;
+    }
+    const size_t B = batch, H = c.hidden_size, I = c.intermediate_size, qd = (size_t)c.n_heads * c.head_dim,
+                 kvd = (size_t)c.n_kv_heads * c.head_dim;
+    const size_t cache = (size_t)c.n_layers * B * max_seq * kvd * 2;
+    int r = Q3_OK;
+    auto A = [&](void **p, size_t bytes) {
+        if (r == Q3_OK) r = alloc(e, p, bytes > 0 ? bytes : 16);
+    };
+    A((void **)&e->x, B * H * 2);
+    A((void **)&e->xb, B * H * 2);
+    A((void **)&e->q, B * qd * 2);
+    A((void **)&e->k, B * kvd * 2);
+    A((void **)&e->v, B * kvd * 2);
+    A((void **)&e->attn_out, B * qd * 2);
+    A((void **)&e->hb, B * I * 2);
+    A((void **)&e->logits, B * (size_t)c.vocab_size * 2);
+    A((void **)&e->key_cache, cache);
+    A((void **)&e->value_cache, cache);
+    const size_t scratch = attention_scratch_layout(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq, nullptr,
+                                                    nullptr, nullptr);
+    A(&e->attn_scratch, scratch);
+    A((void **)&e->next_token, B * 4);
+    A((void **)&e->pos, B * 4);
+    A((void **)&e->out_token, B * 4);
+    A((void **)&e->history, (size_t)(history_cap > 0 ? history_cap : 1) * B * 4);
+    A((void **)&e->step, 16);
+    if (r == Q3_OK) r = record_cuda_error(cudaMallocHost((void **)&e->host_io, 3 * B * sizeof(int)));
+    if (r != Q3_OK) {
+        release(e);
+        return r;
+    }
+    attention_scratch_layout(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq, &e->split, &e->scores,
+                             e->attn_scratch);
+    cudaStream_t s = e->stream;
+    r = record_cuda_error(cudaMemsetAsync(e->attn_scratch, 0, scratch, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->key_cache, 0, cache, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->value_cache, 0, cache, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->next_token, 0, B * 4, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->pos, 0, B * 4, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->step, 0, 16, s));
+    if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(s));
+    if (r != Q3_OK) {
+        release(e);
+        return r;
+    }
+    *out = e;
+    return Q3_OK;
+}
+
+int q3_engine_destroy(q3_engine *e) {
+    if (!e) return Q3_ERR_ARG;
+    cudaStreamSynchronize(e->stream);
+    release(e);
+    return Q3_OK;
+}
+
+int q3_engine_capture(q3_engine *e) {
+    if (!e) return Q3_ERR_ARG;
+    if (e->graph) {
+        cudaGraphExecDestroy(e->graph);
+        e->graph = nullptr;
+    }
+    cudaGraph_t g;
+    int r = record_cuda_error(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    if (r != Q3_OK) return r;
+    const int st = enqueue_step(e);
+    r = record_cuda_error(cudaStreamEndCapture(e->stream, &g));
+    if (st != Q3_OK) {
+        if (r == Q3_OK) cudaGraphDestroy(g);
+        return st;
+    }
+    if (r != Q3_OK) return r;
+    size_t n_nodes = 0;
+    cudaGraphGetNodes(g, nullptr, &n_nodes);
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    int kernels = 0;
+    if (n_nodes && cudaGraphGetNodes(g, nodes.data(), &n_nodes) == cudaSuccess)
+        for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+        }
+    e->graph_kernels = kernels;
+    r = record_cuda_error(cudaGraphInstantiate(&e->graph, g, 0));
+    cudaGraphDestroy(g);
+    return r;
+}
+
+int q3_engine_step(q3_engine *e, int n_steps) {
+    if (!e || n_steps < 0) return Q3_ERR_ARG;
+    for (int i = 0; i < n_steps; i++) {
+        if (e->graph) {
+            int r = record_cuda_error(cudaGraphLaunch(e->graph, e->stream));
+            if (r != Q3_OK) return r;
+        } else {
+            int r = enqueue_step(e);
+            if (r != Q3_OK) return r;
+        }
+    }
+    return Q3_OK;
+}
+
+int q3_engine_set_state(q3_engine *e, const int *tokens, const int *positions) {
+    if (!e || !tokens || !positions) return Q3_ERR_ARG;
+    for (int b = 0; b < e->B; b++) {
+        if (tokens[b] < 0 || tokens[b] >= e->cfg.vocab_size || positions[b] < 0 || positions[b] >= e->max_seq)
+            return Q3_ERR_SHAPE;
+    }
+    int *io = e->host_io;
+    int r = record_cuda_error(cudaStreamSynchronize(e->stream));  // the pinned staging buffer is reused
+    if (r != Q3_OK) return r;
+    memcpy(io, tokens, e->B * sizeof(int));
+    memcpy(io + e->B, positions, e->B * sizeof(int));
+    r = record_cuda_error(cudaMemcpyAsync(e->next_token, io, e->B * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    if (r == Q3_OK)
+        r = record_cuda_error(cudaMemcpyAsync(e->pos, io + e->B, e->B * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    return r;
+}
+
+int q3_engine_forward(q3_engine *e, const int *tokens, const int *positions) {
+    int r = q3_engine_set_state(e, tokens, positions);
+    return r == Q3_OK ? q3_engine_step(e, 1) : r;
+}
+
+int q3_engine_sample_argmax(q3_engine *e, int *tokens_out) {
+    if (!e || !tokens_out) return Q3_ERR_ARG;
+    int *io = e->host_io + 2 * e->B;
+    int r = record_cuda_error(cudaMemcpyAsync(io, e->out_token, e->B * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+    if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(e->stream));
+    if (r == Q3_OK) memcpy(tokens_out, io, e->B * sizeof(int));
+    return r;
+}
+
+int q3_engine_fill_kv_normal(q3_engine *e, int n_positions, unsigned long long seed) {
+    if (!e || n_positions < 0 || n_positions > e->max_seq) return Q3_ERR_ARG;
+    const q3_config &c = e->cfg;
+    const size_t kvd = (size_t)c.n_kv_heads * c.head_dim;
+    const size_t rows = (size_t)n_positions * kvd;
+    for (int l = 0; l < c.n_layers; l++)
+        for (int b = 0; b < e->B; b++) {
+            const size_t off = ((size_t)l * e->B + b) * e->max_seq * kvd;
+            const unsigned long long sk = seed * 1000003ull + (unsigned long long)(l * e->B + b) * 2;
+            TRY(fill_normal(e->key_cache + off, (long long)rows, sk, 0.0f, 1.0f, e->stream));
+            TRY(fill_normal(e->value_cache + off, (long long)rows, sk + 1, 0.0f, 1.0f, e->stream));
+        }
+    return Q3_OK;
+}
+
+int q3_engine_info(const q3_engine *e, q3_engine_buffers *out) {
+    if (!e || !out) return Q3_ERR_ARG;
+    out->x = (q3_bf16 *)e->x;
+    out->logits = (q3_bf16 *)e->logits;
+    out->key_cache = (q3_bf16 *)e->key_cache;
+    out->value_cache = (q3_bf16 *)e->value_cache;
+    out->next_token = e->next_token;
+    out->pos = e->pos;
+    out->out_token = e->out_token;
+    out->history = e->history;
+    out->step = e->step;
+    out->batch = e->B;
+    out->max_seq = e->max_seq;
+    out->history_cap = e->history_cap;
+    out->launches_per_step = e->graph_kernels;
+    return Q3_OK;
+}
+
+int q3_fill_normal_bf16(q3_bf16 *dst, long long n, unsigned long long seed, float mean, float std, void *stream) {
+    int st = check_device();
+    if (st != Q3_OK) return st;
+    return fill_normal((bf16 *)dst, n, seed, mean, std, (cudaStream_t)stream);
+}
+
+}  // extern "C"

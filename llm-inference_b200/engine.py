@@ -1,0 +1,221 @@
+"""Host side of the batched decode engine (csrc/engine.cu) and device-resident weights.
+
+:class:`DeviceWeights` holds a model's tensors in one device buffer at 256-byte aligned
+offsets -- the reference loader's layout (src/loader.cu:143-180, :313-380), where every tensor
+is a pointer into one cudaMalloc'd shard -- read from a checkpoint directory or generated on
+the device from a seed. :class:`Engine` owns a q3_engine: the batched run state, the captured
+decode step and the device-side token loop.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+
+from . import checkpoint as ckpt
+from ._lib import call, load
+
+_B = ctypes.c_void_p
+
+
+class Q3Config(ctypes.Structure):
+    _fields_ = [("hidden_size", ctypes.c_int), ("intermediate_size", ctypes.c_int), ("n_layers", ctypes.c_int),
+                ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+                ("vocab_size", ctypes.c_int), ("rms_norm_eps", ctypes.c_float), ("rope_theta", ctypes.c_float)]
+
+
+class Q3LayerWeights(ctypes.Structure):
+    _fields_ = [(n, _B) for n in ("attn_norm", "wq", "wk", "wv", "q_norm", "k_norm", "wo", "mlp_norm", "w_gate",
+                                  "w_up", "w_down")]
+
+
+class Q3Weights(ctypes.Structure):
+    _fields_ = [("embed", _B), ("layers", ctypes.POINTER(Q3LayerWeights)), ("final_norm", _B), ("lm_head", _B)]
+
+
+class Q3EngineBuffers(ctypes.Structure):
+    _fields_ = [("x", _B), ("logits", _B), ("key_cache", _B), ("value_cache", _B), ("next_token", _B), ("pos", _B),
+                ("out_token", _B), ("history", _B), ("step", _B), ("batch", ctypes.c_int), ("max_seq", ctypes.c_int),
+                ("history_cap", ctypes.c_int), ("launches_per_step", ctypes.c_int)]
+
+
+def q3_config(s: ckpt.Qwen3Shape) -> Q3Config:
+    return Q3Config(s.hidden_size, s.intermediate_size, s.num_hidden_layers, s.num_attention_heads,
+                    s.num_key_value_heads, s.head_dim, s.vocab_size, s.rms_norm_eps, s.rope_theta)
+
+
+class _DevView:
+    """A device pointer as a torch tensor (through __cuda_array_interface__)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def device_view(ptr: int, shape, dtype: str):
+    """torch tensor over device memory owned elsewhere; dtype 'bf16' or 'i32'."""
+    import torch
+    if dtype == "bf16":
+        return torch.as_tensor(_DevView(ptr, shape, "<i2"), device="cuda").view(torch.bfloat16)
+    return torch.as_tensor(_DevView(ptr, shape, "<i4"), device="cuda")
+
+
+_LAYER_SUFFIX = {"attn_norm": "input_layernorm.weight", "wq": "self_attn.q_proj.weight",
+                 "wk": "self_attn.k_proj.weight", "wv": "self_attn.v_proj.weight",
+                 "q_norm": "self_attn.q_norm.weight", "k_norm": "self_attn.k_norm.weight",
+                 "wo": "self_attn.o_proj.weight", "mlp_norm": "post_attention_layernorm.weight",
+                 "w_gate": "mlp.gate_proj.weight", "w_up": "mlp.up_proj.weight", "w_down": "mlp.down_proj.weight"}
+
+
+class DeviceWeights:
+    def __init__(self, shape: ckpt.Qwen3Shape, blob, offsets: dict[str, int]):
+        self.shape = shape
+        self.blob = blob  # torch uint8/int16 tensor on the device that owns the memory
+        self.offsets = offsets
+        base = blob.data_ptr()
+        self.ptr = {k: base + o for k, o in offsets.items()}
+
+    @staticmethod
+    def _layout(shape: ckpt.Qwen3Shape):
+        offsets, off = {}, 0
+        shapes = ckpt.tensor_shapes(shape)
+        for name in sorted(shapes):
+            offsets[name] = off
+            off += (int(np.prod(shapes[name])) * 2 + 255) // 256 * 256
+        return shapes, offsets, off
+
+    @classmethod
+    def from_tensors(cls, shape: ckpt.Qwen3Shape, tensors: dict[str, np.ndarray], device="cuda"):
+        import torch
+        shapes, offsets, total = cls._layout(shape)
+        host = np.zeros(total // 2, np.uint16)
+        for name, o in offsets.items():
+            a = np.ascontiguousarray(tensors[name], np.uint16).reshape(-1)
+            host[o // 2:o // 2 + a.size] = a
+        blob = torch.from_numpy(host.view(np.int16)).to(device)
+        return cls(shape, blob, offsets)
+
+    @classmethod
+    def from_checkpoint(cls, model_dir, device="cuda"):
+        shape, tensors = ckpt.read_checkpoint(model_dir)
+        return cls.from_tensors(shape, tensors, device)
+
+    @classmethod
+    def random(cls, shape: ckpt.Qwen3Shape, seed: int = 0, device="cuda"):
+        """Random-init weights generated on the device (linear N(0, 0.02), norms 1 + N(0, 0.02)),
+        one generator stream per tensor in sorted-name order."""
+        import torch
+        shapes, offsets, total = cls._layout(shape)
+        blob = torch.empty(total // 2, dtype=torch.int16, device=device)
+        obj = cls(shape, blob, offsets)
+        stream = torch.cuda.current_stream().cuda_stream
+        for i, name in enumerate(sorted(shapes)):
+            n = int(np.prod(shapes[name]))
+            mean = 1.0 if ckpt.is_norm(name) else 0.0
+            call("q3_fill_normal_bf16", obj.ptr[name], n, seed * 1000 + i, mean, 0.02, stream)
+        return obj
+
+    def tensor(self, name):
+        return device_view(self.ptr[name], ckpt.tensor_shapes(self.shape)[name], "bf16")
+
+    def q3_weights(self):
+        s = self.shape
+        layers = (Q3LayerWeights * s.num_hidden_layers)()
+        for l in range(s.num_hidden_layers):
+            for field, suffix in _LAYER_SUFFIX.items():
+                setattr(layers[l], field, self.ptr[f"model.layers.{l}.{suffix}"])
+        embed = self.ptr["model.embed_tokens.weight"]
+        lm = embed if s.tie_word_embeddings else self.ptr["lm_head.weight"]
+        w = Q3Weights(embed, layers, self.ptr["model.norm.weight"], lm)
+        w._keep = layers
+        return w
+
+
+class Engine:
+    """Batched greedy decode of `batch` independent sequences (csrc/engine.cu)."""
+
+    def __init__(self, weights: DeviceWeights, batch: int, max_seq: int, history_cap: int = 0,
+                 exact_attention: bool = False, stream=None):
+        import torch
+        load()
+        self.weights = weights
+        self.shape = weights.shape
+        self.batch = batch
+        self.max_seq = max_seq
+        self.cfg = q3_config(self.shape)
+        self._w = weights.q3_weights()
+        if stream is None:  # a dedicated stream: graphs cannot be captured on the legacy stream
+            self._own = torch.cuda.Stream()
+            stream = self._own.cuda_stream
+        self.stream = stream
+        handle = ctypes.c_void_p()
+        call("q3_engine_create", ctypes.byref(self.cfg), ctypes.byref(self._w), batch, max_seq, history_cap,
+             1 if exact_attention else 0, self.stream, ctypes.byref(handle))
+        self.handle = handle
+        info = Q3EngineBuffers()
+        call("q3_engine_info", self.handle, ctypes.byref(info))
+        self.info = info
+
+    # ---- the reference's per-token protocol (host in, host out)
+    def forward(self, tokens, positions):
+        t = (ctypes.c_int * self.batch)(*[int(v) for v in tokens])
+        p = (ctypes.c_int * self.batch)(*[int(v) for v in positions])
+        call("q3_engine_forward", self.handle, t, p)
+
+    def sample_argmax(self) -> list[int]:
+        out = (ctypes.c_int * self.batch)()
+        call("q3_engine_sample_argmax", self.handle, out)
+        return list(out)
+
+    # ---- device-resident loop
+    def set_state(self, tokens, positions):
+        t = (ctypes.c_int * self.batch)(*[int(v) for v in tokens])
+        p = (ctypes.c_int * self.batch)(*[int(v) for v in positions])
+        call("q3_engine_set_state", self.handle, t, p)
+
+    def capture(self):
+        call("q3_engine_capture", self.handle)
+        call("q3_engine_info", self.handle, ctypes.byref(self.info))
+
+    def launches_per_step(self) -> int:
+        return self.info.launches_per_step
+
+    def step(self, n: int = 1):
+        call("q3_engine_step", self.handle, n)
+
+    def fill_kv_normal(self, n_positions: int, seed: int = 0):
+        call("q3_engine_fill_kv_normal", self.handle, n_positions, seed)
+
+    # ---- inspection (each waits for the engine's stream first)
+    def synchronize(self):
+        import torch
+        torch.cuda.ExternalStream(self.stream).synchronize()
+
+    def logits(self):
+        self.synchronize()
+        return device_view(self.info.logits, (self.batch, self.shape.vocab_size), "bf16")
+
+    def history(self):
+        self.synchronize()
+        return device_view(self.info.history, (self.info.history_cap, self.batch), "i32")
+
+    def positions(self):
+        self.synchronize()
+        return device_view(self.info.pos, (self.batch,), "i32")
+
+    def weight_bytes_per_step(self) -> int:
+        return load().q3_weight_bytes_per_step(ctypes.byref(self.cfg))
+
+    def kv_bytes_per_position(self) -> int:
+        return load().q3_kv_bytes_per_position(ctypes.byref(self.cfg))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            call("q3_engine_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

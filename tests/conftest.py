@@ -7,8 +7,9 @@ import pytest
 
 ROOT = Path(__file__).resolve().parents[1]
 PKG_DIR = ROOT / "llm-inference_b200"
-if str(ROOT) not in sys.path:
-    sys.path.insert(0, str(ROOT))
+for _p in (ROOT, ROOT / "oracle", ROOT / "tests" / "golden"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
 
 
 def load_package():
