@@ -153,9 +153,9 @@ int q3_qk_norm_rope_batched(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_b
  * a group size n_heads / n_kv_heads other than 1, 2, 4 or 8). */
 size_t q3_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
 
-/* Split-KV attention per sequence over positions 0..d_pos[b]. `scratch` (size from
- * q3_attention_scratch_bytes) must be zeroed once before the first call; calls leave it ready
- * for the next one. Calls sharing a scratch buffer must not overlap on the GPU. */
+/* Split-KV attention per sequence over positions 0..d_pos[b], with the reference's rounding
+ * points for scores and probabilities; `scratch` (size from q3_attention_scratch_bytes) needs no
+ * initialization. Calls sharing a scratch buffer must not overlap on the GPU. */
 int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache, const q3_bf16 *value_cache,
                          long long cache_seq_stride, void *scratch, const int *d_pos, int batch, int n_heads,
                          int n_kv_heads, int head_dim, int max_seq, float scale, void *stream);

@@ -25,10 +25,9 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
 int sample(int *out, const bf16 *x, int n, float inv_temp, float u, cudaStream_t s);
-int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
-              int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
-              cudaStream_t s);
+int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
+              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 unsigned take_error_gemv();
 unsigned take_error_decode();
 unsigned take_error_attention();
@@ -59,6 +58,7 @@ int current_device() {
 int record_cuda_error(cudaError_t e) {
     if (e == cudaSuccess) return Q3_OK;
     t_last_cuda_error = (int)e;
+    cudaGetLastError();  // a failed call leaves a non-sticky error pending: clear it for other users
     return Q3_ERR_CUDA;
 }
 
@@ -188,7 +188,7 @@ int q3_attention_forward(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
                          const q3_bf16 *value_cache, float *att, int n_heads, int n_kv_heads, int head_dim,
                          const int *d_pos, int max_seq, float scale, void *stream) {
     DEVICE_OR_RETURN();
-    return q3::attention(B(out), CB(q), CB(key_cache), CB(value_cache), att, d_pos, 1,
+    return q3::attention(B(out), CB(q), CB(key_cache), CB(value_cache), att, max_seq, d_pos, 1,
                          (long long)n_heads * head_dim, 0, n_heads, n_kv_heads, head_dim, max_seq, scale,
                          nullptr, S(stream));
 }

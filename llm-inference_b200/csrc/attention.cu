@@ -1,28 +1,29 @@
 // GQA decode attention for sm_100a with the reference's rounding points (src/kernels.cu:439-497).
 //
 // The reference runs one 128-thread block per query head and does everything serially inside
-// it. Here the work is split into two kernels over persistent grids:
+// it. Here the work is split over persistent grids, each CTA taking a contiguous, balanced range
+// of work items, with every global read staged through shared memory by cp.async so that no
+// loop waits on a global round trip per iteration:
 //
-//   scores  (work item = sequence b, kv head, 128 positions): the K rows of the item are staged
-//           in shared memory with cp.async (padded rows, conflict-free), each thread owns one
+//   scores  item = (sequence b, kv head, 256 positions). The item's K rows are staged in shared
+//           memory (padded rows, conflict-free) through a 2-deep ring; each thread owns one
 //           position and computes the dot products of all query heads of the kv group with it,
 //           serially over head_dim as the reference does, so each K row is read once per group.
 //           s = round_bf16(round_bf16(dot) * scale) goes to the scores buffer [b][head][pos].
-//           With split work (below), the last CTA of each (b, kv head) also computes the softmax
-//           statistics of its heads.
-//   pv      (work item = sequence b, kv head, a chunk of positions): probabilities
-//           p = round_bf16(expf(s - max) / sum) as in the reference, then thread d accumulates
-//           p[t] * v[t][d] over the chunk's positions in order with fused multiply-adds, the V
-//           rows staged through a cp.async ring.
+//   stats   one CTA per (b, kv head): the softmax max and sum of each head in the reference's
+//           exact order -- 128 slots, slot j summing positions j, j+128, ... serially, an xor
+//           tree per warp, a serial sum of the four warp totals (block_max / block_sum,
+//           src/kernels.cu:406-436) -- over scores staged in shared memory.
+//   pv      item = (b, kv head, a chunk of positions). Probabilities
+//           p = round_bf16(expf(s - max) / sum) as in the reference (:472-474) from staged score
+//           tiles, then thread d accumulates p[t] * v[t][d] over the chunk in position order with
+//           fused multiply-adds (:478-485), V rows staged through a cp.async ring.
+//   combine sums the chunks' fp32 partial outputs in chunk order and rounds to bf16.
 //
-// The softmax statistics use the reference's exact order: 128 slots, slot j summing positions
-// j, j+128, ... serially, then an xor tree per warp and a serial sum of the four warp totals.
-//
-// Exact mode (one chunk per (b, kv head), used by the drop-in attention_forward): the P.V sum is
-// the reference's single serial chain, so the output is bit-identical; the statistics are
-// computed by each pv CTA itself. Split mode (the decode engine): chunks of a few hundred
-// positions give more parallelism; their fp32 partial sums are added in chunk order by the last
-// CTA of each (b, kv head), which changes only fp32 rounding inside the sum.
+// Exact mode (the drop-in attention_forward): one pv chunk spans all positions, so P.V is the
+// reference's single serial chain, and the pv CTA computes its statistics itself; the output is
+// bit-identical. Split mode (the batched engine): chunks of 512 positions for parallelism; their
+// partial sums are added in chunk order, which changes only fp32 rounding inside the sum.
 #include <math.h>
 
 #include <algorithm>
@@ -34,25 +35,28 @@ namespace {
 
 __device__ unsigned g_dev_error;
 
-constexpr int A_THREADS = 128;   // scores: one thread per position, 128 positions per item
-constexpr int B_THREADS = 128;   // pv: threads over head_dim; 128 slots for the statistics
-constexpr int VT = 64;           // pv: positions per staged V tile
+constexpr int THREADS = 128;     // stats / pv: 128 slots, threads over head_dim
+constexpr int SC_THREADS = 256;  // scores: one thread per position
+constexpr int SC_CHUNK = 256;    // positions per scores item (128 for head_dim > 128)
+constexpr int K_STAGES = 2;
+constexpr int VT = 64;           // positions per staged V tile
 constexpr int V_STAGES = 3;
 constexpr int MAX_B = 1024;      // sequences per launch (prefix table in shared memory)
+constexpr int STATS_SMEM = 160 * 1024;
 
 struct AttnArgs {
     const bf16 *q;        // sequence b: q + b*q_stride, heads concatenated
     const bf16 *kc, *vc;  // sequence b: kc + b*cache_stride, rows [max_seq][kv_dim]
     bf16 *out;            // like q
-    float *scores;        // [B][n_heads][max_seq]
+    float *scores;        // [B][n_heads][ld]
     float *stats;         // split mode: [B][n_heads][2] (max, sum of exp)
     float *partial;       // split mode: [B][n_heads][max_chunks][head_dim]
-    int *count_a;         // split mode: [B][n_kv], zero between launches
-    int *count_b;         // split mode: [B][n_kv], zero between launches
     const int *pos;       // [B]
     long long q_stride, cache_stride;
+    int ld;               // row stride of scores (>= max_seq)
     int B, n_heads, n_kv, head_dim, kv_dim, max_seq;
-    int chunk_b;          // positions per pv item (split mode); ignored in exact mode
+    int chunk_b;          // positions per pv item
+    int sc_chunk;         // positions per scores item
     int max_chunks;       // split mode: capacity of `partial` along the chunk axis
     float scale;
 };
@@ -60,22 +64,29 @@ struct AttnArgs {
 __device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
 }
+__device__ __forceinline__ void cp_async4(void *smem, const void *gmem) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Item table: items of sequence b occupy [prefix[b], prefix[b+1]); n_chunks(b) per kv head.
+// Positions of sequence b, or 0 (no work) for an out-of-range position, which is flagged.
+__device__ __forceinline__ int seq_len(const AttnArgs &a, int b) {
+    const int p = a.pos[b];
+    if (p < 0 || p >= a.max_seq) return 0;
+    return p + 1;
+}
+
+// Item table in shared memory: items of sequence b occupy [prefix[b], prefix[b+1]).
 __device__ int build_prefix(const AttnArgs &a, int chunk, int *prefix) {
     if (threadIdx.x == 0) {
         int total = 0;
         for (int b = 0; b < a.B; b++) {
             prefix[b] = total;
-            int p = a.pos[b];
-            if (p < 0 || p >= a.max_seq) {
-                atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
-                p = -1;  // no work for this sequence
-            }
-            total += a.n_kv * ((p + chunk) / chunk);
+            const int n = seq_len(a, b);
+            if (n == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
+            total += a.n_kv * ((n + chunk - 1) / chunk);
         }
         prefix[a.B] = total;
     }
@@ -83,123 +94,151 @@ __device__ int build_prefix(const AttnArgs &a, int chunk, int *prefix) {
     return prefix[a.B];
 }
 
-__device__ __forceinline__ void find_item(const AttnArgs &a, const int *prefix, int chunk, int item,
-                                          int &b, int &kvh, int &c, int &nc, int &pos) {
-    b = 0;
+struct Item {
+    int b, kvh, c, nc, len;
+};
+
+__device__ __forceinline__ Item find_item(const AttnArgs &a, const int *prefix, int chunk, int item) {
+    Item it;
+    int b = 0;
     while (prefix[b + 1] <= item) b++;
-    pos = a.pos[b];
-    nc = (pos + chunk) / chunk;
+    it.b = b;
+    it.len = seq_len(a, b);
+    it.nc = (it.len + chunk - 1) / chunk;
     const int r = item - prefix[b];
-    kvh = r / nc;
-    c = r - kvh * nc;
+    it.kvh = r / it.nc;
+    it.c = r - it.kvh * it.nc;
+    return it;
 }
 
-// Softmax statistics of the NREP heads of (b, kvh) over positions 0..pos, in the reference's
-// order (block_max / block_sum of src/kernels.cu:406-436 over 128 threads). Needs 128 threads.
+// Copies n scores (floats) from global to shared memory as cp.async groups' members.
+__device__ __forceinline__ void stage_scores(float *dst, const float *src, int n) {
+    if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        const int n4 = n / 4;
+        for (int i = threadIdx.x; i < n4; i += THREADS) cp_async16(dst + 4 * i, src + 4 * i);
+        for (int i = 4 * n4 + threadIdx.x; i < n; i += THREADS) cp_async4(dst + i, src + i);
+    } else {
+        for (int i = threadIdx.x; i < n; i += THREADS) cp_async4(dst + i, src + i);
+    }
+}
+
+// Softmax statistics of the NREP heads of (b, kvh) over positions [0, len) in the reference's
+// order, scores staged through `buf` (cap floats) slice by slice. Needs 128 threads.
 template <int NREP>
-__device__ void softmax_stats(const AttnArgs &a, int b, int kvh, int pos, float *m_out, float *s_out,
-                              float (*red)[NREP]) {
-    const int tid = threadIdx.x;
-    const int lane = tid % 32, warp = tid / 32;
-    const float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP) * a.max_seq;
-    float mx[NREP];
-#pragma unroll
-    for (int h = 0; h < NREP; h++) mx[h] = -INFINITY;
-    for (int t = tid; t <= pos; t += 128)
-#pragma unroll
-        for (int h = 0; h < NREP; h++) mx[h] = fmaxf(mx[h], __ldcg(sc + (size_t)h * a.max_seq + t));
-#pragma unroll
-    for (int h = 0; h < NREP; h++)
-        for (int off = 16; off > 0; off >>= 1) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
-    if (lane == 0)
-#pragma unroll
-        for (int h = 0; h < NREP; h++) red[warp][h] = mx[h];
-    __syncthreads();
+__device__ void softmax_stats(const AttnArgs &a, int b, int kvh, int len, float *buf, int cap, float *m_out,
+                              float *s_out) {
+    __shared__ float red[4][NREP];
+    const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+    const float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP) * a.ld;
+    const int slice = max(THREADS, (cap / NREP) / THREADS * THREADS);  // a multiple of 128 positions
+    float mx[NREP], sm[NREP];
 #pragma unroll
     for (int h = 0; h < NREP; h++) {
-        float r = -INFINITY;
-        for (int w = 0; w < 4; w++) r = fmaxf(r, red[w][h]);
-        mx[h] = r;
+        mx[h] = -INFINITY;
+        sm[h] = 0.0f;
     }
-    __syncthreads();
-    float sm[NREP];
+    for (int pass = 0; pass < 2; pass++) {
+        for (int t0 = 0; t0 < len; t0 += slice) {
+            const int n = min(slice, len - t0);
+            __syncthreads();  // the previous slice has been read
 #pragma unroll
-    for (int h = 0; h < NREP; h++) sm[h] = 0.0f;
-    for (int t = tid; t <= pos; t += 128)
+            for (int h = 0; h < NREP; h++) stage_scores(buf + h * slice, sc + (size_t)h * a.ld + t0, n);
+            cp_async_commit();
+            cp_async_wait<0>();
+            __syncthreads();
+            for (int t = tid; t < n; t += THREADS)
 #pragma unroll
-        for (int h = 0; h < NREP; h++) sm[h] += expf(__ldcg(sc + (size_t)h * a.max_seq + t) - mx[h]);
+                for (int h = 0; h < NREP; h++) {
+                    const float v = buf[h * slice + t];
+                    if (pass == 0) mx[h] = fmaxf(mx[h], v);
+                    else sm[h] += expf(v - mx[h]);
+                }
+        }
+        // block_max / block_sum: xor tree per warp, then the warp totals in warp order
 #pragma unroll
-    for (int h = 0; h < NREP; h++)
-        for (int off = 16; off > 0; off >>= 1) sm[h] += __shfl_xor_sync(0xffffffffu, sm[h], off);
-    if (lane == 0)
+        for (int h = 0; h < NREP; h++) {
+            float v = pass == 0 ? mx[h] : sm[h];
+            for (int off = 16; off > 0; off >>= 1) {
+                const float o = __shfl_xor_sync(0xffffffffu, v, off);
+                v = pass == 0 ? fmaxf(v, o) : v + o;
+            }
+            if (lane == 0) red[warp][h] = v;
+        }
+        __syncthreads();
 #pragma unroll
-        for (int h = 0; h < NREP; h++) red[warp][h] = sm[h];
-    __syncthreads();
+        for (int h = 0; h < NREP; h++) {
+            float r = pass == 0 ? -INFINITY : 0.0f;
+            for (int w = 0; w < 4; w++) r = pass == 0 ? fmaxf(r, red[w][h]) : r + red[w][h];
+            if (pass == 0) mx[h] = r;
+            else sm[h] = r;
+        }
+        __syncthreads();
+    }
 #pragma unroll
     for (int h = 0; h < NREP; h++) {
-        float total = 0.0f;
-        for (int w = 0; w < 4; w++) total += red[w][h];
         m_out[h] = mx[h];
-        s_out[h] = total;
+        s_out[h] = sm[h];
     }
-    __syncthreads();
 }
 
 // ------------------------------------------------------------------ scores
 template <int NREP>
-__global__ void __launch_bounds__(A_THREADS) attn_scores_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(SC_THREADS) attn_scores_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int hd = a.head_dim;
     const int row_elems = hd + 8;  // padded K row: consecutive rows shift by 16 bytes
-    bf16 *ktile[2] = {reinterpret_cast<bf16 *>(smem), reinterpret_cast<bf16 *>(smem) + A_THREADS * row_elems};
-    float *q_s = reinterpret_cast<float *>(smem + 2 * A_THREADS * row_elems * 2);  // [NREP][hd]
+    const int tile_elems = a.sc_chunk * row_elems;
+    bf16 *ktiles = reinterpret_cast<bf16 *>(smem);
+    float *q_s = reinterpret_cast<float *>(smem + (size_t)K_STAGES * tile_elems * 2);  // [NREP][hd]
     int *prefix = reinterpret_cast<int *>(q_s + NREP * hd);
-    __shared__ float red[4][NREP];
-    __shared__ int is_last;
 
     pdl_trigger();
     pdl_wait();
-    const int total = build_prefix(a, A_THREADS, prefix);
+    const int total = build_prefix(a, a.sc_chunk, prefix);
     const int tid = threadIdx.x;
     const int cpr = hd / 8;  // 16-byte chunks per K row
+    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
 
-    auto issue = [&](int item, int buf) {
-        int b, kvh, c, nc, pos;
-        find_item(a, prefix, A_THREADS, item, b, kvh, c, nc, pos);
-        const int t0 = c * A_THREADS;
-        const int rows = min(A_THREADS, pos + 1 - t0);
-        const bf16 *src = a.kc + (size_t)b * a.cache_stride + (size_t)t0 * a.kv_dim + (size_t)kvh * hd;
-        for (int j = tid; j < rows * cpr; j += A_THREADS) {
+    auto issue = [&](int item, int stage) {
+        const Item it = find_item(a, prefix, a.sc_chunk, item);
+        const int t0 = it.c * a.sc_chunk;
+        const int rows = min(a.sc_chunk, it.len - t0);
+        const bf16 *src = a.kc + (size_t)it.b * a.cache_stride + (size_t)t0 * a.kv_dim + (size_t)it.kvh * hd;
+        bf16 *dst = ktiles + (size_t)stage * tile_elems;
+        for (int j = tid; j < rows * cpr; j += SC_THREADS) {
             const int r = j / cpr, ch = j - r * cpr;
-            cp_async16(ktile[buf] + r * row_elems + ch * 8, src + (size_t)r * a.kv_dim + ch * 8);
+            cp_async16(dst + r * row_elems + ch * 8, src + (size_t)r * a.kv_dim + ch * 8);
         }
-        cp_async_commit();
     };
 
-    int item = blockIdx.x;
-    if (item < total) issue(item, 0);
-    int buf = 0;
-    for (; item < total; item += gridDim.x, buf ^= 1) {
-        int b, kvh, c, nc, pos;
-        find_item(a, prefix, A_THREADS, item, b, kvh, c, nc, pos);
-        const int next = item + gridDim.x;
-        if (next < total) {
-            issue(next, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
+    // prologue: K_STAGES - 1 items in flight
+    for (int s = 0; s < K_STAGES - 1; s++) {
+        if (i0 + s < i1) issue(i0 + s, s);
+        cp_async_commit();
+    }
+    int cur_b = -1, cur_kvh = -1;
+    for (int item = i0; item < i1; item++) {
+        const int k = item - i0;
+        if (item + K_STAGES - 1 < i1) issue(item + K_STAGES - 1, (k + K_STAGES - 1) % K_STAGES);
+        cp_async_commit();
+        const Item it = find_item(a, prefix, a.sc_chunk, item);
+        if (it.b != cur_b || it.kvh != cur_kvh) {  // q of the group's heads, as fp32
+            __syncthreads();
+            const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
+            for (int j = tid; j < NREP * hd; j += SC_THREADS) q_s[j] = __bfloat162float(qg[j]);
+            cur_b = it.b;
+            cur_kvh = it.kvh;
         }
-        // q of the group's heads as fp32
-        const bf16 *qg = a.q + (size_t)b * a.q_stride + (size_t)kvh * NREP * hd;
-        for (int j = tid; j < NREP * hd; j += A_THREADS) q_s[j] = __bfloat162float(qg[j]);
+        cp_async_wait<K_STAGES - 1>();
         __syncthreads();
 
-        const int t = c * A_THREADS + tid;
-        if (t <= pos) {
+        const int t = it.c * a.sc_chunk + tid;
+        if (tid < a.sc_chunk && t < it.len) {
             float acc[NREP];
 #pragma unroll
             for (int h = 0; h < NREP; h++) acc[h] = 0.0f;
-            const bf16 *krow = ktile[buf] + tid * row_elems;
+            const bf16 *krow = ktiles + (size_t)(k % K_STAGES) * tile_elems + tid * row_elems;
             for (int ch = 0; ch < cpr; ch++) {
                 const bf16x8 kv = lds128(krow + ch * 8);
                 float kf[8];
@@ -223,97 +262,95 @@ __global__ void __launch_bounds__(A_THREADS) attn_scores_kernel(const __grid_con
                     acc[h] = __fmaf_rn(q1.w, kf[7], acc[h]);
                 }
             }
-            float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP) * a.max_seq + t;
+            float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld + t;
 #pragma unroll
-            for (int h = 0; h < NREP; h++) sc[(size_t)h * a.max_seq] = round_bf16(round_bf16(acc[h]) * a.scale);
+            for (int h = 0; h < NREP; h++) sc[(size_t)h * a.ld] = round_bf16(round_bf16(acc[h]) * a.scale);
         }
+        __syncthreads();  // this stage is refilled K_STAGES - 1 items later
+    }
+    cp_async_wait<0>();
+}
 
-        if (a.count_a != nullptr) {
-            // split mode: the last CTA of (b, kvh) computes the softmax statistics
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) {
-                const int done = atomicAdd(a.count_a + b * a.n_kv + kvh, 1);
-                is_last = done == nc - 1;
-            }
-            __syncthreads();
-            if (is_last) {
-                __threadfence();
-                float m[NREP], s[NREP];
-                softmax_stats<NREP>(a, b, kvh, pos, m, s, red);
-                if (tid < NREP) {
-                    float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + tid) * 2;
-                    st[0] = m[tid];
-                    st[1] = s[tid];
-                }
-                if (tid == 0) a.count_a[b * a.n_kv + kvh] = 0;
-            }
-        }
-        __syncthreads();  // ktile[buf] and q_s are reused by the next item
+// ------------------------------------------------------------------ stats (split mode)
+template <int NREP>
+__global__ void __launch_bounds__(THREADS) attn_stats_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x / a.n_kv, kvh = blockIdx.x % a.n_kv;
+    const int len = seq_len(a, b);
+    if (len == 0) return;
+    float m[NREP], s[NREP];
+    softmax_stats<NREP>(a, b, kvh, len, reinterpret_cast<float *>(smem), STATS_SMEM / 4, m, s);
+    if (threadIdx.x < NREP) {
+        float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + threadIdx.x) * 2;
+        st[0] = m[threadIdx.x];
+        st[1] = s[threadIdx.x];
     }
 }
 
 // ------------------------------------------------------------------ pv
 template <int NREP, int DPT>
-__global__ void __launch_bounds__(B_THREADS) attn_pv_kernel(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int hd = a.head_dim;
-    bf16 *vtile = reinterpret_cast<bf16 *>(smem);                       // [V_STAGES][VT][hd]
-    float *p_s = reinterpret_cast<float *>(vtile + V_STAGES * VT * hd);  // [V_STAGES][NREP][VT]
-    int *prefix = reinterpret_cast<int *>(p_s + V_STAGES * NREP * VT);
-    __shared__ float red[4][NREP];
+    bf16 *vtile = reinterpret_cast<bf16 *>(smem);                          // [V_STAGES][VT][hd]
+    float *s_tile = reinterpret_cast<float *>(vtile + V_STAGES * VT * hd);  // [V_STAGES][NREP][VT]
+    float *p_tile = s_tile + V_STAGES * NREP * VT;                          // [NREP][VT]
+    int *prefix = reinterpret_cast<int *>(p_tile + NREP * VT);
     __shared__ float m_s[NREP], s_s[NREP];
-    __shared__ int is_last;
 
     pdl_trigger();
     pdl_wait();
-    const bool split = a.count_b != nullptr;
-    const int chunk = split ? a.chunk_b : a.max_seq;
+    const bool split = a.stats != nullptr;
+    const int chunk = a.chunk_b;
     const int total = build_prefix(a, chunk, prefix);
     const int tid = threadIdx.x;
     const int cpr = hd / 8;
+    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
 
-    for (int item = blockIdx.x; item < total; item += gridDim.x) {
-        int b, kvh, c, nc, pos;
-        find_item(a, prefix, chunk, item, b, kvh, c, nc, pos);
-        const int t0 = c * chunk;
-        const int t1 = min(t0 + chunk, pos + 1);
+    for (int item = i0; item < i1; item++) {
+        const Item it = find_item(a, prefix, chunk, item);
+        const int t0 = it.c * chunk;
+        const int t1 = min(t0 + chunk, it.len);
         const int n_tiles = (t1 - t0 + VT - 1) / VT;
-        const float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP) * a.max_seq;
-        const bf16 *vsrc = a.vc + (size_t)b * a.cache_stride + (size_t)kvh * hd;
+        const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
+        const bf16 *vsrc = a.vc + (size_t)it.b * a.cache_stride + (size_t)it.kvh * hd;
 
         auto issue = [&](int tile) {
             const int st = tile % V_STAGES;
             const int tt0 = t0 + tile * VT;
             const int rows = min(VT, t1 - tt0);
             bf16 *dst = vtile + st * VT * hd;
-            for (int j = tid; j < rows * cpr; j += B_THREADS) {
+            for (int j = tid; j < rows * cpr; j += THREADS) {
                 const int r = j / cpr, ch = j - r * cpr;
                 cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv_dim + ch * 8);
             }
-            cp_async_commit();
+#pragma unroll
+            for (int h = 0; h < NREP; h++) stage_scores(s_tile + (st * NREP + h) * VT, sc + (size_t)h * a.ld + tt0, rows);
         };
-        // V loads do not depend on the statistics: start the ring first
-        for (int tile = 0; tile < V_STAGES - 1; tile++) {
-            if (tile < n_tiles) issue(tile);
-            else cp_async_commit();
-        }
 
         if (split) {
             if (tid < NREP) {
-                const float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + tid) * 2;
+                const float *st = a.stats + ((size_t)it.b * a.n_heads + it.kvh * NREP + tid) * 2;
                 m_s[tid] = __ldcg(st);
                 s_s[tid] = __ldcg(st + 1);
             }
-            __syncthreads();
         } else {
+            // exact mode: this CTA is the only one of (b, kvh); the V ring memory stages the scores
             float m[NREP], s[NREP];
-            softmax_stats<NREP>(a, b, kvh, pos, m, s, red);
+            const int cap = (V_STAGES * VT * hd * 2) / 4;
+            softmax_stats<NREP>(a, it.b, it.kvh, it.len, reinterpret_cast<float *>(vtile), cap, m, s);
             if (tid < NREP) {
                 m_s[tid] = m[tid];
                 s_s[tid] = s[tid];
             }
-            __syncthreads();
+        }
+        __syncthreads();
+        for (int tile = 0; tile < V_STAGES - 1; tile++) {
+            if (tile < n_tiles) issue(tile);
+            cp_async_commit();
         }
 
         float acc[NREP][DPT];
@@ -324,103 +361,116 @@ __global__ void __launch_bounds__(B_THREADS) attn_pv_kernel(const __grid_constan
 
         for (int tile = 0; tile < n_tiles; tile++) {
             const int st = tile % V_STAGES;
-            const int tt0 = t0 + tile * VT;
-            const int rows = min(VT, t1 - tt0);
-            // probabilities of this tile
-            float *pt = p_s + st * NREP * VT;
-            for (int j = tid; j < NREP * VT; j += B_THREADS) {
-                const int h = j / VT, r = j - h * VT;
-                if (r < rows) {
-                    const float sv = __ldcg(sc + (size_t)h * a.max_seq + tt0 + r);
-                    pt[h * VT + r] = round_bf16(expf(sv - m_s[h]) / s_s[h]);
-                }
-            }
+            const int rows = min(VT, t1 - (t0 + tile * VT));
             if (tile + V_STAGES - 1 < n_tiles) issue(tile + V_STAGES - 1);
-            else cp_async_commit();
+            cp_async_commit();
             cp_async_wait<V_STAGES - 1>();
+            __syncthreads();
+            // probabilities of this tile (src/kernels.cu:472-474)
+            const float *stile = s_tile + st * NREP * VT;
+            for (int j = tid; j < NREP * VT; j += THREADS) {
+                const int h = j / VT, r = j - h * VT;
+                if (r < rows) p_tile[j] = round_bf16(expf(stile[j] - m_s[h]) / s_s[h]);
+            }
             __syncthreads();
             const bf16 *vt = vtile + st * VT * hd;
 #pragma unroll
             for (int k = 0; k < DPT; k++) {
-                const int d = tid + k * B_THREADS;
+                const int d = tid + k * THREADS;
                 if (d < hd) {
+#pragma unroll 8
                     for (int r = 0; r < rows; r++) {
                         const float v = __bfloat162float(vt[r * hd + d]);
 #pragma unroll
-                        for (int h = 0; h < NREP; h++) acc[h][k] = __fmaf_rn(pt[h * VT + r], v, acc[h][k]);
+                        for (int h = 0; h < NREP; h++) acc[h][k] = __fmaf_rn(p_tile[h * VT + r], v, acc[h][k]);
                     }
                 }
             }
-            __syncthreads();  // the stage is refilled V_STAGES - 1 tiles later
+            __syncthreads();  // the stage and p_tile are rewritten next
         }
         cp_async_wait<0>();
 
-        const size_t out_base = (size_t)b * a.q_stride + (size_t)kvh * NREP * hd;
-        if (!split || nc == 1) {
+        const size_t out_base = (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
+        if (it.nc == 1) {
 #pragma unroll
             for (int h = 0; h < NREP; h++)
 #pragma unroll
                 for (int k = 0; k < DPT; k++) {
-                    const int d = tid + k * B_THREADS;
+                    const int d = tid + k * THREADS;
                     if (d < hd) a.out[out_base + (size_t)h * hd + d] = __float2bfloat16(acc[h][k]);
                 }
-            if (split && tid == 0) a.count_b[b * a.n_kv + kvh] = 0;  // single chunk: nothing to combine
         } else {
-            float *part = a.partial + ((size_t)b * a.n_heads + kvh * NREP) * a.max_chunks * hd;
+            float *part = a.partial + ((size_t)it.b * a.n_heads + it.kvh * NREP) * a.max_chunks * hd;
 #pragma unroll
             for (int h = 0; h < NREP; h++)
 #pragma unroll
                 for (int k = 0; k < DPT; k++) {
-                    const int d = tid + k * B_THREADS;
-                    if (d < hd) part[((size_t)h * a.max_chunks + c) * hd + d] = acc[h][k];
+                    const int d = tid + k * THREADS;
+                    if (d < hd) part[((size_t)h * a.max_chunks + it.c) * hd + d] = acc[h][k];
                 }
-            __threadfence();
-            __syncthreads();
-            if (tid == 0) is_last = atomicAdd(a.count_b + b * a.n_kv + kvh, 1) == nc - 1;
-            __syncthreads();
-            if (is_last) {
-                __threadfence();
-#pragma unroll
-                for (int h = 0; h < NREP; h++)
-#pragma unroll
-                    for (int k = 0; k < DPT; k++) {
-                        const int d = tid + k * B_THREADS;
-                        if (d < hd) {
-                            float o = 0.0f;
-                            for (int cc = 0; cc < nc; cc++) o += __ldcg(part + ((size_t)h * a.max_chunks + cc) * hd + d);
-                            a.out[out_base + (size_t)h * hd + d] = __float2bfloat16(o);
-                        }
-                    }
-                if (tid == 0) a.count_b[b * a.n_kv + kvh] = 0;
-            }
         }
-        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------ combine (split mode)
+__global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.y, h = blockIdx.x;
+    const int len = seq_len(a, b);
+    const int nc = (len + a.chunk_b - 1) / a.chunk_b;
+    if (nc <= 1) return;  // the pv kernel wrote the output directly
+    const float *part = a.partial + ((size_t)b * a.n_heads + h) * a.max_chunks * a.head_dim;
+    for (int d = threadIdx.x; d < a.head_dim; d += blockDim.x) {
+        float o = 0.0f;
+        int c = 0;
+        for (; c + 4 <= nc; c += 4) {  // four loads in flight, added in chunk order
+            const float p0 = __ldcg(part + (size_t)(c + 0) * a.head_dim + d);
+            const float p1 = __ldcg(part + (size_t)(c + 1) * a.head_dim + d);
+            const float p2 = __ldcg(part + (size_t)(c + 2) * a.head_dim + d);
+            const float p3 = __ldcg(part + (size_t)(c + 3) * a.head_dim + d);
+            o += p0;
+            o += p1;
+            o += p2;
+            o += p3;
+        }
+        for (; c < nc; c++) o += __ldcg(part + (size_t)c * a.head_dim + d);
+        a.out[(size_t)b * a.q_stride + (size_t)h * a.head_dim + d] = __float2bfloat16(o);
     }
 }
 
 template <int NREP>
 int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     const int nsm = num_sms();
-    const size_t a_smem = (size_t)2 * A_THREADS * (a.head_dim + 8) * 2 + (size_t)NREP * a.head_dim * 4 +
-                          (size_t)(a.B + 1) * 4;
-    const size_t b_smem = (size_t)V_STAGES * VT * a.head_dim * 2 + (size_t)V_STAGES * NREP * VT * 4 +
-                          (size_t)(a.B + 1) * 4;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_kernel<NREP>), a_smem));
-    // grids: enough CTAs to cover the largest number of items, at most a few per SM
-    const long long max_items_a = (long long)a.B * a.n_kv * ((a.max_seq + A_THREADS - 1) / A_THREADS);
-    const int grid_a = (int)std::min<long long>(max_items_a, 4LL * nsm);
-    Q3_TRY_LAUNCH(launch(attn_scores_kernel<NREP>, dim3(grid_a), dim3(A_THREADS), a_smem, s, 1, a));
-    const bool split = a.count_b != nullptr;
-    const long long chunk = split ? a.chunk_b : a.max_seq;
-    const long long max_items_b = (long long)a.B * a.n_kv * ((a.max_seq + chunk - 1) / chunk);
-    const int grid_b = (int)std::min<long long>(max_items_b, 4LL * nsm);
-    if (dpt == 1) {
-        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_kernel<NREP, 1>), b_smem));
-        Q3_TRY_LAUNCH(launch(attn_pv_kernel<NREP, 1>, dim3(grid_b), dim3(B_THREADS), b_smem, s, 1, a));
-    } else {
-        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_kernel<NREP, 2>), b_smem));
-        Q3_TRY_LAUNCH(launch(attn_pv_kernel<NREP, 2>, dim3(grid_b), dim3(B_THREADS), b_smem, s, 1, a));
+    const bool split = a.stats != nullptr;
+    const size_t prefix_bytes = (size_t)(a.B + 1) * 4;
+    // scores
+    const size_t sc_smem = (size_t)K_STAGES * a.sc_chunk * (a.head_dim + 8) * 2 + (size_t)NREP * a.head_dim * 4 + prefix_bytes;
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_kernel<NREP>), sc_smem));
+    const long long max_sc = (long long)a.B * a.n_kv * ((a.max_seq + a.sc_chunk - 1) / a.sc_chunk);
+    const int per_sm = std::max(1, (int)((200 * 1024) / sc_smem));
+    const int grid_sc = (int)std::min<long long>(max_sc, (long long)nsm * per_sm);
+    Q3_TRY_LAUNCH(launch(attn_scores_kernel<NREP>, dim3(grid_sc), dim3(SC_THREADS), sc_smem, s, 1, a));
+    // stats
+    if (split) {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), STATS_SMEM));
+        Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), (size_t)STATS_SMEM, s, 1, a));
     }
+    // pv
+    const size_t pv_smem = (size_t)V_STAGES * VT * a.head_dim * 2 + (size_t)V_STAGES * NREP * VT * 4 +
+                           (size_t)NREP * VT * 4 + prefix_bytes;
+    const long long max_pv = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
+    const int per_sm_pv = std::max(1, (int)((200 * 1024) / pv_smem));
+    const int grid_pv = (int)std::min<long long>(max_pv, (long long)nsm * per_sm_pv);
+    if (dpt == 1) {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_kernel<NREP, 1>), pv_smem));
+        Q3_TRY_LAUNCH(launch(attn_pv_kernel<NREP, 1>, dim3(grid_pv), dim3(THREADS), pv_smem, s, 1, a));
+    } else {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_kernel<NREP, 2>), pv_smem));
+        Q3_TRY_LAUNCH(launch(attn_pv_kernel<NREP, 2>, dim3(grid_pv), dim3(THREADS), pv_smem, s, 1, a));
+    }
+    // combine
+    if (split) Q3_TRY_LAUNCH(launch(attn_combine_kernel, dim3(a.n_heads, a.B), dim3(128), 0, s, 1, a));
     return Q3_OK;
 }
 
@@ -443,16 +493,16 @@ int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int 
     return Q3_OK;
 }
 
-// Attention over n_rows sequences. Exact mode when split == nullptr; otherwise `split` holds the
-// split-mode scratch (stats, partial, count_a, count_b, chunk_b, max_chunks).
-
-int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
-              int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
-              cudaStream_t s) {
+// Attention over n_rows sequences. `scores` has rows of `ld` floats per (sequence, head). Exact
+// mode when split == nullptr; otherwise `split` holds the split-mode scratch (stats, partial,
+// chunk_b, max_chunks; the counters are unused).
+int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
+              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s) {
     if (!out || !q || !key_cache || !value_cache || !scores || !pos) return Q3_ERR_ARG;
     int st = attention_check(n_heads, n_kv_heads, head_dim, max_seq, n_rows);
     if (st != Q3_OK) return st;
+    if (ld < max_seq) return Q3_ERR_SHAPE;
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
     if (!al(key_cache) || !al(value_cache) || (cache_stride * 2) % 16 != 0) return Q3_ERR_ALIGN;
     AttnArgs a = {};
@@ -461,6 +511,7 @@ int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value
     a.vc = value_cache;
     a.out = out;
     a.scores = scores;
+    a.ld = ld;
     a.pos = pos;
     a.q_stride = q_stride;
     a.cache_stride = cache_stride;
@@ -471,13 +522,13 @@ int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value
     a.kv_dim = n_kv_heads * head_dim;
     a.max_seq = max_seq;
     a.scale = scale;
+    a.chunk_b = max_seq;  // exact mode: one chunk spans every position
+    a.sc_chunk = head_dim <= 128 ? SC_CHUNK : SC_CHUNK / 2;  // K ring within shared memory
     if (split) {
-        if (!split->stats || !split->partial || !split->count_a || !split->count_b) return Q3_ERR_ARG;
+        if (!split->stats || !split->partial) return Q3_ERR_ARG;
         if (split->chunk_b <= 0 || (long long)split->chunk_b * split->max_chunks < max_seq) return Q3_ERR_SHAPE;
         a.stats = split->stats;
         a.partial = split->partial;
-        a.count_a = split->count_a;
-        a.count_b = split->count_b;
         a.chunk_b = split->chunk_b;
         a.max_chunks = split->max_chunks;
     }

@@ -32,10 +32,9 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
-int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
-              int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
-              cudaStream_t s);
+int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
+              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
 
 // ---------------------------------------------------------------- batched projections
@@ -97,9 +96,11 @@ int proj_gate_up(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x,
 
 // ---------------------------------------------------------------- attention scratch
 
-// Split-mode scratch layout: scores [B][H][max_seq] f32 | stats [B][H][2] f32 |
-// partial [B][H][max_chunks][hd] f32 | count_a [B][n_kv] i32 | count_b [B][n_kv] i32.
+// Split-mode scratch layout: scores [B][H][ld] f32 (ld = max_seq rounded up to 4, so score rows
+// stay 16-byte aligned) | stats [B][H][2] f32 | partial [B][H][max_chunks][hd] f32.
 constexpr int ATTN_CHUNK = 512;
+
+int score_ld(int max_seq) { return (max_seq + 3) / 4 * 4; }
 
 size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, AttnSplit *sp,
                                 float **scores, void *base) {
@@ -110,18 +111,16 @@ size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head
         off += (bytes + 255) / 256 * 256;
         return o;
     };
-    const size_t o_scores = take((size_t)batch * n_heads * max_seq * 4);
+    const size_t o_scores = take((size_t)batch * n_heads * score_ld(max_seq) * 4);
     const size_t o_stats = take((size_t)batch * n_heads * 2 * 4);
     const size_t o_part = take((size_t)batch * n_heads * max_chunks * head_dim * 4);
-    const size_t o_ca = take((size_t)batch * n_kv_heads * 4);
-    const size_t o_cb = take((size_t)batch * n_kv_heads * 4);
     if (base && sp && scores) {
         char *p = static_cast<char *>(base);
         *scores = reinterpret_cast<float *>(p + o_scores);
         sp->stats = reinterpret_cast<float *>(p + o_stats);
         sp->partial = reinterpret_cast<float *>(p + o_part);
-        sp->count_a = reinterpret_cast<int *>(p + o_ca);
-        sp->count_b = reinterpret_cast<int *>(p + o_cb);
+        sp->count_a = nullptr;
+        sp->count_b = nullptr;
         sp->chunk_b = ATTN_CHUNK;
         sp->max_chunks = max_chunks;
     }
@@ -201,7 +200,7 @@ int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
     AttnSplit sp;
     float *scores = nullptr;
     attention_scratch_layout(batch, n_heads, n_kv_heads, head_dim, max_seq, &sp, &scores, scratch);
-    return attention(B(out), CB(q), CB(key_cache), CB(value_cache), scores, d_pos, batch,
+    return attention(B(out), CB(q), CB(key_cache), CB(value_cache), scores, score_ld(max_seq), d_pos, batch,
                      (long long)n_heads * head_dim, cache_seq_stride, n_heads, n_kv_heads, head_dim, max_seq, scale,
                      &sp, S(stream));
 }

@@ -187,9 +187,8 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Scratch of the split-KV attention (attention.cu): softmax statistics, per-chunk partial
-// outputs and two per-(sequence, kv head) counters that must be zero before the first call
-// (the kernels return them to zero).
+// Scratch of the split-KV attention (attention.cu): softmax statistics and per-chunk partial
+// outputs (the counters are unused).
 struct AttnSplit {
     float *stats;
     float *partial;

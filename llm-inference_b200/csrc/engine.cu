@@ -38,11 +38,11 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
-int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads,
-              int n_kv_heads, int head_dim, int max_seq, float scale, const AttnSplit *split,
-              cudaStream_t s);
+int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
+              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
+int score_ld(int max_seq);
 size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, AttnSplit *sp,
                                 float **scores, void *base);
 int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s);
@@ -106,8 +106,8 @@ int enqueue_step(q3_engine *e) {
         TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, e->pos, B, qd,
                          kvd, seq_stride, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps,
                          c.rope_theta, nullptr, nullptr, s));
-        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, e->pos, B, qd, seq_stride, c.n_heads, c.n_kv_heads,
-                      c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
+        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), e->pos, B, qd, seq_stride,
+                      c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
         TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, B, H, qd, nullptr, s));
         TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, B, H, c.rms_norm_eps, s));
         TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, B, I, H, nullptr, nullptr, s));

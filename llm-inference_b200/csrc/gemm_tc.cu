@@ -19,9 +19,14 @@
 //                    SwiGLU (:277-286). The single accumulator is reused tile after tile; the
 //                    producer keeps prefetching the next tile's stages meanwhile.
 //
-// Work: weight rows are cut into tiles of R <= 128 rows, R chosen so that the tiles divide
-// evenly over the SMs; a persistent grid of at most one CTA per SM walks the tiles. The gate
-// and up projections share a tile (two accumulators side by side in TMEM).
+// Work: weight rows are cut into tiles of R <= 128 rows and K into S slices; a tile's S slices
+// run on the S CTAs of one thread-block cluster. R and S are chosen so that tiles x S fill the
+// SMs in one wave with as many weight bytes per pipeline stage as possible (o_proj and down,
+// 2560 rows: S = 4). With S > 1 each CTA stages its fp32 partial tile in shared memory and,
+// after a cluster barrier, reduces its share of the tile's rows over the S CTAs' partials
+// (distributed shared memory, in rank order) before the epilogue. With S = 1 a persistent
+// grid walks the tiles. The gate and up projections share a tile (two accumulators side by
+// side in TMEM).
 //
 // Arithmetic note: the fp32 sums run in the tensor core's order, not the reference's
 // lane-strided order, so results can differ from the batch-1 kernels in the last bf16 bit.
@@ -30,10 +35,14 @@
 
 #include <string.h>
 
+#include <cooperative_groups.h>
+
 #include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace q3 {
 namespace {
@@ -59,6 +68,7 @@ struct TcArgs {
     int n_tiles;
     int R;                         // rows per tile (TMA box rows)
     int K, nk;                     // columns and number of BK steps
+    int splits;                    // S: CTAs of a cluster sharing a tile along K
     int B, Bp;                     // batch rows and MMA N
     int stages;
     int stage_bytes;
@@ -167,8 +177,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
 
-    const int my_tiles = a.n_tiles > (int)blockIdx.x ? (a.n_tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    const int total_steps = my_tiles * a.nk;
+    // split-K: the S CTAs of a cluster share tile blockIdx.x / S, rank r takes K steps [k0, k1)
+    const int S_split = a.splits;
+    const int rank = S_split > 1 ? (int)cg::this_cluster().block_rank() : 0;
+    const int tile_base = S_split > 1 ? (int)blockIdx.x / S_split : (int)blockIdx.x;
+    const int tile_stride = S_split > 1 ? (int)gridDim.x / S_split : (int)gridDim.x;
+    const int k0 = a.nk * rank / S_split, k1 = a.nk * (rank + 1) / S_split;
+    const int nks = k1 - k0;
+    const int my_tiles = a.n_tiles > tile_base ? (a.n_tiles - 1 - tile_base) / tile_stride + 1 : 0;
+    const int total_steps = my_tiles * nks;
     const uint32_t a_bytes = (uint32_t)a.R * BK * 2;
     const uint32_t x_bytes = (uint32_t)a.Bp * BK * 2;
     bool ok = true;
@@ -180,8 +197,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         auto stage_x = [&](int s) { return smem + (size_t)s * a.stage_bytes + (size_t)NA * A_TILE_BYTES; };
         auto issue_weights = [&](int it) {
             const int s = it % S;
-            const int t = blockIdx.x + (it / a.nk) * gridDim.x;
-            const int ks = it % a.nk;
+            const int t = tile_base + (it / nks) * tile_stride;
+            const int ks = k0 + it % nks;
             int mat, row0;
             tile_coords(a, t, mat, row0);
             mbar_arrive_expect_tx(&full[s], NA * a_bytes + x_bytes);
@@ -192,7 +209,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 tma_load_2d(stage_a(s, 0), maps[mat], ks * BK, row0, &full[s]);
             }
         };
-        auto issue_x = [&](int it) { tma_load_2d(stage_x(it % S), &tmX, (it % a.nk) * BK, 0, &full[it % S]); };
+        auto issue_x = [&](int it) { tma_load_2d(stage_x(it % S), &tmX, (k0 + it % nks) * BK, 0, &full[it % S]); };
         const int pre = min(S, total_steps);
         for (int it = 0; it < pre; it++) issue_weights(it);  // weights do not depend on the previous kernel
         pdl_wait();
@@ -217,7 +234,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 break;
             }
             tc_fence_after();
-            for (int ks = 0; ks < a.nk; ks++, it++) {
+            for (int ks = 0; ks < nks; ks++, it++) {
                 const int s = it % S;
                 if (!mbar_wait(&full[s], (it / S) & 1, &g_dev_error)) {
                     ok = false;
@@ -239,8 +256,69 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
 
+    __syncwarp();
+    if (S_split > 1) {
+        // ---------------- split-K epilogue: partial tile -> shared memory -> cluster reduction
+        // (one tile per cluster; the pipeline ring is idle and is reused for the partial tile)
+        const int ld = NA * a.Bp + 1;  // padded row: conflict-free column writes
+        float *part = reinterpret_cast<float *>(smem);
+        if (warp >= 2 && my_tiles > 0) {
+            const int quarter = warp % 4;
+            const int row_local = quarter * 32 + lane;
+            const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+            if (!mbar_wait(acc_full, 0, &g_dev_error)) ok = false;
+            tc_fence_after();
+            for (int c0 = 0; c0 < NA * a.Bp; c0 += 8) {
+                float acc[8];
+                tmem_ld8(lane_addr + c0, acc);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 8; j++) part[row_local * ld + c0 + j] = acc[j];
+            }
+            tc_fence_before();
+        }
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (my_tiles > 0) {
+            pdl_wait();
+            int mat, row0;
+            tile_coords(a, tile_base, mat, row0);
+            bf16 *o = EPI == QKV ? (mat == 0 ? a.out0 : mat == 1 ? a.out1 : a.out2) : a.out0;
+            const long long ostride = a.rows[mat];
+            const int r_lo = a.R * rank / S_split, r_hi = a.R * (rank + 1) / S_split;
+            const int nr = r_hi - r_lo;
+            const float *peer[8];
+            for (int q = 0; q < S_split; q++) peer[q] = cluster.map_shared_rank(part, q);
+            for (int i = threadIdx.x; i < nr * a.B; i += TC_THREADS) {
+                const int b = i / nr, rl = r_lo + i % nr;  // consecutive threads: consecutive rows
+                const int m = row0 + rl;
+                if (m >= a.rows[mat]) continue;
+                float acc = 0.0f, acc2 = 0.0f;
+                for (int q = 0; q < S_split; q++) {
+                    acc += peer[q][rl * ld + b];
+                    if (EPI == GATE_UP) acc2 += peer[q][rl * ld + a.Bp + b];
+                }
+                const size_t idx = (size_t)b * ostride + m;
+                if (EPI == PLAIN || EPI == QKV) {
+                    o[idx] = __float2bfloat16(acc);
+                } else if (EPI == RESIDUAL) {
+                    const bf16 y = __float2bfloat16(acc);
+                    if (a.tap0) a.tap0[idx] = y;
+                    o[idx] = __float2bfloat16(__bfloat162float(o[idx]) + __bfloat162float(y));
+                } else {
+                    const bf16 gate = __float2bfloat16(acc), up = __float2bfloat16(acc2);
+                    if (a.tap0) {
+                        a.tap0[idx] = gate;
+                        a.tap1[idx] = up;
+                    }
+                    const float gv = __bfloat162float(gate), uv = __bfloat162float(up);
+                    o[idx] = __float2bfloat16(round_bf16(gv / (1.0f + expf(-gv))) * uv);
+                }
+            }
+        }
+        cluster.sync();  // every CTA's partial tile stays alive until all ranks have read it
+    } else if (warp >= 2) {
     // ---------------- epilogue (warps 2-5, one accumulator row per thread)
-    if (warp >= 2) {
     pdl_wait();
     const int quarter = warp % 4;
     const int row_local = quarter * 32 + lane;
@@ -251,7 +329,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             break;
         }
         tc_fence_after();
-        const int t = blockIdx.x + tl * gridDim.x;
+        const int t = tile_base + tl * tile_stride;
         int mat, row0;
         tile_coords(a, t, mat, row0);
         const int m = row0 + row_local;
@@ -346,20 +424,39 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
     }
     if (total_rows == 0) return Q3_OK;
     const int nsm = num_sms();
-    // rows per tile: as even as possible over the SMs, at most 128
-    const long long waves = (total_rows + (long long)nsm * TILE_M - 1) / ((long long)nsm * TILE_M);
-    int R = (int)std::min<long long>(TILE_M, (total_rows + nsm * waves - 1) / (nsm * waves));
-    R = std::min(TILE_M, std::max(R, 32));  // tiny matrices: fewer, fuller tiles
-    for (;; R++) {
+    a.nk = (a.K + BK - 1) / BK;
+    auto tiles_for = [&](int R) {
         int n = 0;
         for (int i = 0; i < n_mat; i++) n += (a.rows[i] + R - 1) / R;
-        if (n <= nsm * waves || R == TILE_M) break;
+        return n;
+    };
+    // Plan (R rows per tile, S K-slices): all tiles x S CTAs in one wave, minimizing the K steps
+    // of one CTA weighted by its rows (rows below 64 count as 64: small tiles waste stages).
+    int R = 0, S_best = 1;
+    long long best = -1;
+    for (int S = 1; S <= 8 && S <= a.nk; S++) {
+        const int slots = nsm / S;
+        int r = std::max(8, (int)((total_rows + slots - 1) / slots));
+        while (r <= TILE_M && tiles_for(r) > slots) r++;
+        if (r > TILE_M) continue;
+        const long long cost = (long long)std::max(r, 64) * ((a.nk + S - 1) / S);
+        if (best < 0 || cost < best) {
+            best = cost;
+            R = r;
+            S_best = S;
+        }
+    }
+    if (R == 0) {  // more rows than one wave holds: persistent CTAs over 128-row-or-less tiles
+        const long long waves = (total_rows + (long long)nsm * TILE_M - 1) / ((long long)nsm * TILE_M);
+        R = (int)std::min<long long>(TILE_M, (total_rows + nsm * waves - 1) / (nsm * waves));
+        while (R < TILE_M && tiles_for(R) > nsm * waves) R++;
+        S_best = 1;
     }
     a.R = R;
+    a.splits = S_best;
     a.tile_start[0] = 0;
     for (int i = 0; i < 3; i++) a.tile_start[i + 1] = a.tile_start[i] + (i < n_mat ? (a.rows[i] + R - 1) / R : 0);
     a.n_tiles = a.tile_start[3];
-    a.nk = (a.K + BK - 1) / BK;
     a.Bp = std::max(16, (a.B + 15) / 16 * 16);
     a.stage_bytes = NA * A_TILE_BYTES + a.Bp * BK * 2;
     a.stages = (int)std::min<size_t>(MAX_STAGES, (SMEM_BUDGET - 1024 - 256) / a.stage_bytes);
@@ -381,10 +478,15 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
     }
     if (!make_map(&mx, x, a.B, a.K, a.Bp)) return Q3_ERR_ARG;
 
+    // split-K reuses the ring for the fp32 partial tile [128][NA*Bp + 1]
+    if (a.splits > 1 && (size_t)a.stages * a.stage_bytes < (size_t)TILE_M * (NA * a.Bp + 1) * 4) {
+        a.stages = (int)(((size_t)TILE_M * (NA * a.Bp + 1) * 4 + a.stage_bytes - 1) / a.stage_bytes);
+        if ((size_t)a.stages * a.stage_bytes + 1024 + 256 > SMEM_MAX) return Q3_ERR_SHAPE;
+    }
     const size_t smem = 1024 + (size_t)a.stages * a.stage_bytes + (2 * a.stages + 2) * 8 + 16;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(tc_gemm_kernel<EPI>), smem));
-    const int grid = std::min(nsm, a.n_tiles);
-    Q3_TRY_LAUNCH(launch(tc_gemm_kernel<EPI>, dim3(grid), dim3(TC_THREADS), smem, stream, 1, m0, m1, m2, mx, a));
+    const int grid = a.splits > 1 ? a.n_tiles * a.splits : std::min(nsm, a.n_tiles);
+    Q3_TRY_LAUNCH(launch(tc_gemm_kernel<EPI>, dim3(grid), dim3(TC_THREADS), smem, stream, a.splits, m0, m1, m2, mx, a));
     return Q3_OK;
 }
 
