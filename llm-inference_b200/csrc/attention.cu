@@ -24,11 +24,20 @@
 // reference's single serial chain, and the pv CTA computes its statistics itself; the output is
 // bit-identical. Split mode (the batched engine): chunks of 512 positions for parallelism; their
 // partial sums are added in chunk order, which changes only fp32 rounding inside the sum.
+//
+// Split mode also moves the dot products onto the tensor cores (attn_scores_tc_kernel):
+// D[128 positions x 16] = K_tile[128 x head_dim] . Q^T, with the K tile and the group's query
+// rows loaded by TMA (128-byte swizzle), one tcgen05.mma per 16 head dims into a double-buffered
+// TMEM accumulator, and the same score rounding in the epilogue. The tensor core sums a dot in
+// its own order, so a score can differ from the serial sum's rounding in rare cases. Its P.V
+// (attn_pv_vec_kernel) gives each thread two adjacent dims (bf16x2 loads) of one half of the
+// positions, all query heads of the group at once (one vector load of their probabilities).
 #include <math.h>
 
 #include <algorithm>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace q3 {
 namespace {
@@ -412,6 +421,246 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
     }
 }
 
+// ------------------------------------------------------------------ scores on tcgen05 (split mode)
+constexpr int TC_TILE = 128;        // positions per item = MMA M
+constexpr int TC_N = 16;            // MMA N: query heads of the group, padded
+constexpr int TC_STAGES = 4;
+constexpr int TC_THREADS = 192;     // producer warp, MMA warp, 4 epilogue warps
+
+struct ScoreTcPlan {
+    int halves;         // head_dim / 64
+    int k_rows_per_seq; // rows of the K map per sequence (cache_stride / kv_dim)
+    int stage_bytes;
+    uint32_t idesc;
+};
+
+template <int NREP>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    attn_scores_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
+                          const __grid_constant__ AttnArgs a, const __grid_constant__ ScoreTcPlan pl) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int kbytes = TC_TILE * 128;  // one 64-dim half of the K tile
+    const int qbytes = TC_N * 128;     // one 64-dim half of the query rows
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)TC_STAGES * pl.stage_bytes);
+    uint64_t *empty = full + TC_STAGES;
+    uint64_t *acc_full = empty + TC_STAGES;    // [2]
+    uint64_t *acc_empty = acc_full + 2;        // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    int *prefix = reinterpret_cast<int *>(tmem_slot + 4);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < TC_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        fence_barrier_init();
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmQ);
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(32)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
+    pdl_wait();  // positions and the newest cache rows come from the previous kernels
+    // prefix table (thread 0 of the CTA builds it; build_prefix synchronizes all threads)
+    const int total = build_prefix(a, TC_TILE, prefix);
+    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    const int n = i1 - i0;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- producer
+        int k = 0;
+        for (; k < n; k++) {
+            const int st = k % TC_STAGES;
+            if (k >= TC_STAGES && !mbar_wait(&empty[st], ((k / TC_STAGES) - 1) & 1, &g_dev_error)) break;
+            const Item it = find_item(a, prefix, TC_TILE, i0 + k);
+            unsigned char *base = smem + (size_t)st * pl.stage_bytes;
+            mbar_arrive_expect_tx(&full[st], (uint32_t)pl.halves * (kbytes + qbytes));
+            const int krow = it.b * pl.k_rows_per_seq + it.c * TC_TILE;
+            const int qrow = it.b * a.n_heads + it.kvh * NREP;
+            for (int h = 0; h < pl.halves; h++) {
+                tma_load_2d(base + h * kbytes, &tmK, it.kvh * a.head_dim + h * TMA_BK, krow, &full[st]);
+                tma_load_2d(base + pl.halves * kbytes + h * qbytes, &tmQ, h * TMA_BK, qrow, &full[st]);
+            }
+        }
+        for (int j = max(0, k - TC_STAGES); j < k; j++) mbar_wait(&full[j % TC_STAGES], (j / TC_STAGES) & 1, &g_dev_error);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer: 16 head dims per instruction
+        for (int k = 0; k < n; k++) {
+            const int st = k % TC_STAGES, buf = k & 1;
+            if (k >= 2 && !mbar_wait(&acc_empty[buf], ((k >> 1) - 1) & 1, &g_dev_error)) break;
+            if (!mbar_wait(&full[st], (k / TC_STAGES) & 1, &g_dev_error)) break;
+            tc_fence_after();
+            const uint32_t kb = smem_u32(smem + (size_t)st * pl.stage_bytes);
+            const uint32_t qb = kb + pl.halves * kbytes;
+            for (int kk = 0; kk < pl.halves * 4; kk++) {
+                const int h = kk >> 2, o = (kk & 3) * 32;
+                mma_bf16(tmem_base + buf * TC_N, smem_desc_sw128(kb + h * kbytes + o), smem_desc_sw128(qb + h * qbytes + o),
+                         pl.idesc, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(&empty[st]);
+            mma_commit(&acc_full[buf]);
+        }
+    } else if (warp >= 2) {
+        // ---------------- epilogue: one position per thread
+        const int quarter = warp % 4;
+        const int row = quarter * 32 + lane;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        for (int k = 0; k < n; k++) {
+            const int buf = k & 1;
+            if (!mbar_wait(&acc_full[buf], (k >> 1) & 1, &g_dev_error)) break;
+            tc_fence_after();
+            float acc[8];
+            tmem_ld8(lane_addr + buf * TC_N, acc);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+            const Item it = find_item(a, prefix, TC_TILE, i0 + k);
+            const int t = it.c * TC_TILE + row;
+            if (t < it.len) {
+                float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld + t;
+#pragma unroll
+                for (int h = 0; h < NREP; h++) sc[(size_t)h * a.ld] = round_bf16(round_bf16(acc[h]) * a.scale);
+            }
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(32) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ pv, vectorized (split mode)
+// Thread t covers dims 2*(t % P), 2*(t % P) + 1 (P = head_dim / 2 threads per group) for the
+// positions of group t / P: group g takes the g-th of G = 128 / P contiguous slices of every V
+// tile. The G partial sums are added in group order at the end of the item.
+template <int NREP>
+__global__ void __launch_bounds__(THREADS) attn_pv_vec_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int hd = a.head_dim;
+    const int P = hd / 2, G = THREADS / P;
+    bf16 *vtile = reinterpret_cast<bf16 *>(smem);                          // [V_STAGES][VT][hd]
+    float *s_tile = reinterpret_cast<float *>(vtile + V_STAGES * VT * hd);  // [V_STAGES][NREP][VT]
+    float *p_tile = s_tile + V_STAGES * NREP * VT;                          // [VT][NREP]
+    float *red = p_tile + VT * NREP;                                        // [G][NREP][hd]
+    int *prefix = reinterpret_cast<int *>(red + G * NREP * hd);
+    __shared__ float m_s[NREP], s_s[NREP];
+
+    pdl_trigger();
+    pdl_wait();
+    const int chunk = a.chunk_b;
+    const int total = build_prefix(a, chunk, prefix);
+    const int tid = threadIdx.x;
+    const int cpr = hd / 8;
+    const int pair = tid % P, grp = tid / P;
+    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    const int sub = VT / G;  // positions of a tile per group
+
+    for (int item = i0; item < i1; item++) {
+        const Item it = find_item(a, prefix, chunk, item);
+        const int t0 = it.c * chunk;
+        const int t1 = min(t0 + chunk, it.len);
+        const int n_tiles = (t1 - t0 + VT - 1) / VT;
+        const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
+        const bf16 *vsrc = a.vc + (size_t)it.b * a.cache_stride + (size_t)it.kvh * hd;
+        auto issue = [&](int tile) {
+            const int st = tile % V_STAGES;
+            const int tt0 = t0 + tile * VT;
+            const int rows = min(VT, t1 - tt0);
+            bf16 *dst = vtile + st * VT * hd;
+            for (int j = tid; j < rows * cpr; j += THREADS) {
+                const int r = j / cpr, ch = j - r * cpr;
+                cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv_dim + ch * 8);
+            }
+#pragma unroll
+            for (int h = 0; h < NREP; h++) stage_scores(s_tile + (st * NREP + h) * VT, sc + (size_t)h * a.ld + tt0, rows);
+        };
+        if (tid < NREP) {
+            const float *st = a.stats + ((size_t)it.b * a.n_heads + it.kvh * NREP + tid) * 2;
+            m_s[tid] = __ldcg(st);
+            s_s[tid] = __ldcg(st + 1);
+        }
+        __syncthreads();
+        for (int tile = 0; tile < V_STAGES - 1; tile++) {
+            if (tile < n_tiles) issue(tile);
+            cp_async_commit();
+        }
+        float acc[NREP][2];
+#pragma unroll
+        for (int h = 0; h < NREP; h++) acc[h][0] = acc[h][1] = 0.0f;
+        for (int tile = 0; tile < n_tiles; tile++) {
+            const int st = tile % V_STAGES;
+            const int rows = min(VT, t1 - (t0 + tile * VT));
+            if (tile + V_STAGES - 1 < n_tiles) issue(tile + V_STAGES - 1);
+            cp_async_commit();
+            cp_async_wait<V_STAGES - 1>();
+            __syncthreads();
+            const float *stile = s_tile + st * NREP * VT;
+            for (int j = tid; j < NREP * VT; j += THREADS) {
+                const int h = j / VT, r = j - h * VT;
+                if (r < rows) p_tile[r * NREP + h] = round_bf16(expf(stile[j] - m_s[h]) / s_s[h]);
+            }
+            __syncthreads();
+            const bf16 *vt = vtile + st * VT * hd + 2 * pair;
+            const int r0 = grp * sub, r1 = min(r0 + sub, rows);
+#pragma unroll 4
+            for (int r = r0; r < r1; r++) {
+                const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(vt + r * hd));
+                float pv[NREP];
+                if (NREP == 4) {
+                    const float4 p4 = *reinterpret_cast<const float4 *>(p_tile + r * 4);
+                    pv[0] = p4.x; pv[1] = p4.y; pv[2] = p4.z; pv[3] = p4.w;
+                } else {
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) pv[h] = p_tile[r * NREP + h];
+                }
+#pragma unroll
+                for (int h = 0; h < NREP; h++) {
+                    acc[h][0] = __fmaf_rn(pv[h], v.x, acc[h][0]);
+                    acc[h][1] = __fmaf_rn(pv[h], v.y, acc[h][1]);
+                }
+            }
+            __syncthreads();
+        }
+        cp_async_wait<0>();
+        // groups' partial sums, added in group order
+#pragma unroll
+        for (int h = 0; h < NREP; h++) {
+            red[(grp * NREP + h) * hd + 2 * pair] = acc[h][0];
+            red[(grp * NREP + h) * hd + 2 * pair + 1] = acc[h][1];
+        }
+        __syncthreads();
+        const size_t out_base = (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
+        float *part = a.partial + ((size_t)it.b * a.n_heads + it.kvh * NREP) * a.max_chunks * hd;
+        for (int j = tid; j < NREP * hd; j += THREADS) {
+            const int h = j / hd, d = j - h * hd;
+            float o = 0.0f;
+            for (int g = 0; g < G; g++) o += red[(g * NREP + h) * hd + d];
+            if (it.nc == 1) a.out[out_base + (size_t)h * hd + d] = __float2bfloat16(o);
+            else part[((size_t)h * a.max_chunks + it.c) * hd + d] = o;
+        }
+        __syncthreads();
+    }
+}
+
 // ------------------------------------------------------------------ combine (split mode)
 __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant__ AttnArgs a) {
     pdl_trigger();
@@ -440,10 +689,53 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
 }
 
 template <int NREP>
+int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
+    ScoreTcPlan pl;
+    pl.halves = a.head_dim / TMA_BK;
+    pl.k_rows_per_seq = (int)(a.cache_stride / a.kv_dim);
+    pl.stage_bytes = pl.halves * (TC_TILE * 128 + TC_N * 128);
+    // kind::f16: fp32 accumulate, bf16 A and B, both K-major, N = 16, M = 128
+    pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_TILE >> 4) << 24);
+    CUtensorMap mk, mq;
+    if (!make_map_strided(&mk, a.kc, (long long)a.B * pl.k_rows_per_seq, a.kv_dim, a.kv_dim, TC_TILE)) return Q3_ERR_ARG;
+    if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TC_N)) return Q3_ERR_ARG;
+    const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)(a.B + 1) * 4;
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_tc_kernel<NREP>), smem));
+    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + TC_TILE - 1) / TC_TILE);
+    const int grid = (int)std::min<long long>(max_items, num_sms());
+    Q3_TRY_LAUNCH(launch(attn_scores_tc_kernel<NREP>, dim3(grid), dim3(TC_THREADS), smem, s, 1, mk, mq, a, pl));
+    return Q3_OK;
+}
+
+// The tensor-core scores need whole 64-dim halves, contiguous per-sequence caches in kv_dim rows,
+// and a packed q; the vectorized pv needs an even head_dim that splits 128 threads into groups.
+bool split_fast_path(const AttnArgs &a) {
+    return a.head_dim % TMA_BK == 0 && a.head_dim <= 256 && a.cache_stride % a.kv_dim == 0 &&
+           a.q_stride == (long long)a.n_heads * a.head_dim && 128 % (a.head_dim / 2) == 0 &&
+           (a.cache_stride / a.kv_dim) * (long long)a.B < (1LL << 31);
+}
+
+template <int NREP>
 int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     const int nsm = num_sms();
     const bool split = a.stats != nullptr;
     const size_t prefix_bytes = (size_t)(a.B + 1) * 4;
+    if (split && split_fast_path(a)) {
+        int st = launch_scores_tc<NREP>(a, s);
+        if (st != Q3_OK) return st;
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), STATS_SMEM));
+        Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), (size_t)STATS_SMEM, s, 1, a));
+        const int G = THREADS / (a.head_dim / 2);
+        const size_t pv_smem = (size_t)V_STAGES * VT * a.head_dim * 2 + (size_t)V_STAGES * NREP * VT * 4 +
+                               (size_t)VT * NREP * 4 + (size_t)G * NREP * a.head_dim * 4 + prefix_bytes;
+        const long long max_pv = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
+        const int per_sm_pv = std::max(1, (int)((200 * 1024) / pv_smem));
+        const int grid_pv = (int)std::min<long long>(max_pv, (long long)nsm * per_sm_pv);
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_vec_kernel<NREP>), pv_smem));
+        Q3_TRY_LAUNCH(launch(attn_pv_vec_kernel<NREP>, dim3(grid_pv), dim3(THREADS), pv_smem, s, 1, a));
+        Q3_TRY_LAUNCH(launch(attn_combine_kernel, dim3(a.n_heads, a.B), dim3(128), 0, s, 1, a));
+        return Q3_OK;
+    }
     // scores
     const size_t sc_smem = (size_t)K_STAGES * a.sc_chunk * (a.head_dim + 8) * 2 + (size_t)NREP * a.head_dim * 4 + prefix_bytes;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_kernel<NREP>), sc_smem));

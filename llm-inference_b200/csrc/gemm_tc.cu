@@ -39,8 +39,10 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -53,8 +55,8 @@ constexpr int TC_THREADS = 192;  // producer warp, MMA warp, 4 epilogue warps
 constexpr int EPI_THREADS = 128;
 constexpr int BK = 64;            // K per stage: 64 bf16 = one 128-byte swizzle row
 constexpr int TILE_M = 128;       // MMA M
-constexpr int A_TILE_BYTES = TILE_M * BK * 2;  // 16 KB
-constexpr int MAX_STAGES = 8;
+constexpr int MAX_STAGES = 12;
+constexpr int KSUB = 4;           // 64-column sub-tiles per stage: 512 contiguous bytes per weight row
 constexpr size_t SMEM_BUDGET = 112 * 1024;  // leaves room for a co-resident successor kernel
 constexpr size_t SMEM_MAX = 220 * 1024;
 
@@ -67,64 +69,16 @@ struct TcArgs {
     int tile_start[4];             // first tile of each matrix in the tile list
     int n_tiles;
     int R;                         // rows per tile (TMA box rows)
-    int K, nk;                     // columns and number of BK steps
+    int K, nk;                     // columns and number of pipeline stages of ksub * BK columns
+    int ksub;                      // 64-column sub-tiles per stage (adjacent: longer DRAM runs per row)
     int splits;                    // S: CTAs of a cluster sharing a tile along K
     int B, Bp;                     // batch rows and MMA N
     int stages;
     int stage_bytes;
+    int a_tile_bytes;              // shared bytes of one weight tile: R rows rounded up to 8, x 128
     uint32_t idesc;
     uint32_t tmem_cols;
 };
-
-// ---------------------------------------------------------------- PTX wrappers
-
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
-__device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
-}
-
-// K-major operand in the 128-byte swizzle layout: rows of 128 bytes, 8-row groups 1024 bytes
-// apart (stride byte offset), leading byte offset 16 bytes, descriptor version 1 (sm_100).
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
-    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                         uint32_t accumulate) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-        : "memory");
-}
-
-__device__ __forceinline__ void mma_commit(uint64_t *bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
-    uint32_t r[8];
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr)
-                 : "memory");
-#pragma unroll
-    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------- kernel
 
@@ -193,23 +147,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0 && lane == 0) {
         // ---------------- producer
         const CUtensorMap *maps[3] = {&tmA0, &tmA1, &tmA2};
-        auto stage_a = [&](int s, int i) { return smem + (size_t)s * a.stage_bytes + (size_t)i * A_TILE_BYTES; };
-        auto stage_x = [&](int s) { return smem + (size_t)s * a.stage_bytes + (size_t)NA * A_TILE_BYTES; };
+        // stage layout: [A sub-tiles 0..ksub-1][A1 sub-tiles (gate_up)][X sub-tiles 0..ksub-1]
+        auto stage_a = [&](int s, int i, int j) {
+            return smem + (size_t)s * a.stage_bytes + (size_t)(i * a.ksub + j) * a.a_tile_bytes;
+        };
+        auto stage_x = [&](int s, int j) {
+            return smem + (size_t)s * a.stage_bytes + (size_t)NA * a.ksub * a.a_tile_bytes + (size_t)j * x_bytes;
+        };
+        auto subs_of = [&](int ks) { return min(a.ksub, (a.K - ks * a.ksub * BK + BK - 1) / BK); };
         auto issue_weights = [&](int it) {
             const int s = it % S;
             const int t = tile_base + (it / nks) * tile_stride;
             const int ks = k0 + it % nks;
+            const int nsub = subs_of(ks);
             int mat, row0;
             tile_coords(a, t, mat, row0);
-            mbar_arrive_expect_tx(&full[s], NA * a_bytes + x_bytes);
-            if (EPI == GATE_UP) {
-                tma_load_2d(stage_a(s, 0), &tmA0, ks * BK, row0, &full[s]);
-                tma_load_2d(stage_a(s, 1), &tmA1, ks * BK, row0, &full[s]);
-            } else {
-                tma_load_2d(stage_a(s, 0), maps[mat], ks * BK, row0, &full[s]);
+            mbar_arrive_expect_tx(&full[s], nsub * (NA * a_bytes + x_bytes));
+            for (int j = 0; j < nsub; j++) {
+                const int col = (ks * a.ksub + j) * BK;
+                if (EPI == GATE_UP) {
+                    tma_load_2d(stage_a(s, 0, j), &tmA0, col, row0, &full[s]);
+                    tma_load_2d(stage_a(s, 1, j), &tmA1, col, row0, &full[s]);
+                } else {
+                    tma_load_2d(stage_a(s, 0, j), maps[mat], col, row0, &full[s]);
+                }
             }
         };
-        auto issue_x = [&](int it) { tma_load_2d(stage_x(it % S), &tmX, (k0 + it % nks) * BK, 0, &full[it % S]); };
+        auto issue_x = [&](int it) {
+            const int ks = k0 + it % nks;
+            const int nsub = subs_of(ks);
+            for (int j = 0; j < nsub; j++) tma_load_2d(stage_x(it % S, j), &tmX, (ks * a.ksub + j) * BK, 0, &full[it % S]);
+        };
         const int pre = min(S, total_steps);
         for (int it = 0; it < pre; it++) issue_weights(it);  // weights do not depend on the previous kernel
         pdl_wait();
@@ -241,14 +209,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t xs = smem_u32(smem + (size_t)s * a.stage_bytes + (size_t)NA * A_TILE_BYTES);
+                const int kglob = k0 + ks;
+                const int nsub = min(a.ksub, (a.K - kglob * a.ksub * BK + BK - 1) / BK);
+                const uint32_t sbase = smem_u32(smem + (size_t)s * a.stage_bytes);
+                const uint32_t xbase = sbase + NA * a.ksub * a.a_tile_bytes;
+                for (int j = 0; j < nsub; j++) {
+                    const uint32_t xs = xbase + j * (uint32_t)(a.Bp * BK * 2);
 #pragma unroll
-                for (int i = 0; i < NA; i++) {
-                    const uint32_t as = smem_u32(smem + (size_t)s * a.stage_bytes + (size_t)i * A_TILE_BYTES);
+                    for (int i = 0; i < NA; i++) {
+                        const uint32_t as = sbase + (i * a.ksub + j) * a.a_tile_bytes;
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; kk++)
-                        mma_bf16(tmem_base + i * a.Bp, smem_desc_sw128(as + kk * 32), smem_desc_sw128(xs + kk * 32),
-                                 a.idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+                        for (int kk = 0; kk < BK / 16; kk++)
+                            mma_bf16(tmem_base + i * a.Bp, smem_desc_sw128(as + kk * 32), smem_desc_sw128(xs + kk * 32),
+                                     a.idesc, (ks > 0 || j > 0 || kk > 0) ? 1u : 0u);
+                    }
                 }
                 mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
             }
@@ -289,30 +263,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int nr = r_hi - r_lo;
             const float *peer[8];
             for (int q = 0; q < S_split; q++) peer[q] = cluster.map_shared_rank(part, q);
-            for (int i = threadIdx.x; i < nr * a.B; i += TC_THREADS) {
-                const int b = i / nr, rl = r_lo + i % nr;  // consecutive threads: consecutive rows
-                const int m = row0 + rl;
-                if (m >= a.rows[mat]) continue;
-                float acc = 0.0f, acc2 = 0.0f;
-                for (int q = 0; q < S_split; q++) {
-                    acc += peer[q][rl * ld + b];
-                    if (EPI == GATE_UP) acc2 += peer[q][rl * ld + a.Bp + b];
+            // Items (row, b), consecutive threads on consecutive rows; EB items per thread at a
+            // time with every load (partials of all ranks, the residual) issued before any use.
+            constexpr int EB = 4;
+            const int n_items = nr * a.B;
+            for (int base = 0; base < n_items; base += EB * TC_THREADS) {
+                float acc[EB], acc2[EB], xr[EB];
+                int idx_m[EB], idx_b[EB];
+#pragma unroll
+                for (int e = 0; e < EB; e++) {
+                    const int i = base + e * TC_THREADS + (int)threadIdx.x;
+                    idx_b[e] = i < n_items ? i / nr : -1;
+                    idx_m[e] = i < n_items ? r_lo + i % nr : 0;
+                    if (idx_b[e] >= 0 && row0 + idx_m[e] >= a.rows[mat]) idx_b[e] = -1;
+                    acc[e] = acc2[e] = 0.0f;
+                    xr[e] = 0.0f;
+                    if (EPI == RESIDUAL && idx_b[e] >= 0)
+                        xr[e] = __bfloat162float(o[(size_t)idx_b[e] * ostride + row0 + idx_m[e]]);
                 }
-                const size_t idx = (size_t)b * ostride + m;
-                if (EPI == PLAIN || EPI == QKV) {
-                    o[idx] = __float2bfloat16(acc);
-                } else if (EPI == RESIDUAL) {
-                    const bf16 y = __float2bfloat16(acc);
-                    if (a.tap0) a.tap0[idx] = y;
-                    o[idx] = __float2bfloat16(__bfloat162float(o[idx]) + __bfloat162float(y));
-                } else {
-                    const bf16 gate = __float2bfloat16(acc), up = __float2bfloat16(acc2);
-                    if (a.tap0) {
-                        a.tap0[idx] = gate;
-                        a.tap1[idx] = up;
+                for (int q = 0; q < S_split; q++) {
+#pragma unroll
+                    for (int e = 0; e < EB; e++) {
+                        if (idx_b[e] < 0) continue;
+                        acc[e] += peer[q][idx_m[e] * ld + idx_b[e]];
+                        if (EPI == GATE_UP) acc2[e] += peer[q][idx_m[e] * ld + a.Bp + idx_b[e]];
                     }
-                    const float gv = __bfloat162float(gate), uv = __bfloat162float(up);
-                    o[idx] = __float2bfloat16(round_bf16(gv / (1.0f + expf(-gv))) * uv);
+                }
+#pragma unroll
+                for (int e = 0; e < EB; e++) {
+                    if (idx_b[e] < 0) continue;
+                    const size_t idx = (size_t)idx_b[e] * ostride + row0 + idx_m[e];
+                    if (EPI == PLAIN || EPI == QKV) {
+                        o[idx] = __float2bfloat16(acc[e]);
+                    } else if (EPI == RESIDUAL) {
+                        const bf16 y = __float2bfloat16(acc[e]);
+                        if (a.tap0) a.tap0[idx] = y;
+                        o[idx] = __float2bfloat16(xr[e] + __bfloat162float(y));
+                    } else {
+                        const bf16 gate = __float2bfloat16(acc[e]), up = __float2bfloat16(acc2[e]);
+                        if (a.tap0) {
+                            a.tap0[idx] = gate;
+                            a.tap1[idx] = up;
+                        }
+                        const float gv = __bfloat162float(gate), uv = __bfloat162float(up);
+                        o[idx] = __float2bfloat16(round_bf16(gv / (1.0f + expf(-gv))) * uv);
+                    }
                 }
             }
         }
@@ -382,33 +377,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
 // ---------------------------------------------------------------- host side
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void *p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// 2-D bf16 map over a row-major [rows, cols] matrix with a [box_rows, 64] box, 128-byte swizzle.
-bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_rows) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS;
-}
-
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 template <int EPI>
@@ -424,22 +392,92 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
     }
     if (total_rows == 0) return Q3_OK;
     const int nsm = num_sms();
-    a.nk = (a.K + BK - 1) / BK;
+    a.Bp = std::max(16, (a.B + 15) / 16 * 16);
+    const int k64 = (a.K + BK - 1) / BK;  // 64-column steps
+    // wide stages for long contiguous weight runs, narrower when the activation tiles grow
+    a.ksub = std::min(a.Bp <= 64 ? KSUB : a.Bp <= 128 ? 2 : 1, k64);
+    a.nk = (k64 + a.ksub - 1) / a.ksub;
     auto tiles_for = [&](int R) {
         int n = 0;
         for (int i = 0; i < n_mat; i++) n += (a.rows[i] + R - 1) / R;
         return n;
     };
-    // Plan (R rows per tile, S K-slices): all tiles x S CTAs in one wave, minimizing the K steps
-    // of one CTA weighted by its rows (rows below 64 count as 64: small tiles waste stages).
+    // Plan (R rows per tile, S K-slices): every cluster of S CTAs resident in one wave (checked
+    // with the occupancy API, since clusters must fit inside one GPC), minimizing the work of the
+    // busiest SM: K stages of its CTAs times their rows (rows below 64 count as 64).
+    auto smem_for = [&](int R_, int S_, int *stages_out) {
+        const int at = (R_ + 7) / 8 * 8 * BK * 2;
+        const int sb = a.ksub * (NA * at + a.Bp * BK * 2);
+        int st = (int)std::min<size_t>(MAX_STAGES, (SMEM_BUDGET - 1024 - 256) / sb);
+        st = std::max(st, 2);
+        if (S_ > 1 && (size_t)st * sb < (size_t)TILE_M * (NA * a.Bp + 1) * 4)
+            st = (int)(((size_t)TILE_M * (NA * a.Bp + 1) * 4 + sb - 1) / sb);
+        // the M = 128 MMA reads up to (128 - R) rows past a weight tile: slack beyond the last stage
+        const int over = (TILE_M - (R_ + 7) / 8 * 8) * BK * 2 - a.ksub * a.Bp * BK * 2;
+        if (stages_out) *stages_out = st;
+        return (size_t)1024 + (size_t)st * sb + 256 + (size_t)std::max(over, 0);
+    };
+    auto resident = [&](int S_, size_t smem_) {
+        int n = 0;
+        if (smem_ > SMEM_MAX) return 0;
+        if (allow_smem(reinterpret_cast<const void *>(tc_gemm_kernel<EPI>), smem_) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        if (S_ == 1) {
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, tc_gemm_kernel<EPI>, TC_THREADS, smem_) != cudaSuccess)
+                n = 1;
+            cudaGetLastError();
+            return n * nsm;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(S_ * nsm);
+        cfg.blockDim = dim3(TC_THREADS);
+        cfg.dynamicSmemBytes = smem_;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = S_;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, tc_gemm_kernel<EPI>, &cfg) != cudaSuccess) n = 0;
+        cudaGetLastError();
+        return n;
+    };
     int R = 0, S_best = 1;
     long long best = -1;
-    for (int S = 1; S <= 8 && S <= a.nk; S++) {
-        const int slots = nsm / S;
-        int r = std::max(8, (int)((total_rows + slots - 1) / slots));
-        while (r <= TILE_M && tiles_for(r) > slots) r++;
-        if (r > TILE_M) continue;
-        const long long cost = (long long)std::max(r, 64) * ((a.nk + S - 1) / S);
+    bool cached = false;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const long long key[7] = {EPI, a.rows[0], a.rows[1], a.rows[2], a.K, a.B, dev};
+    static std::mutex plan_mu;
+    static std::vector<std::pair<std::vector<long long>, std::pair<int, int>>> plans;
+    {
+        std::lock_guard<std::mutex> lock(plan_mu);
+        for (auto &pl : plans)
+            if (std::equal(pl.first.begin(), pl.first.end(), key)) {
+                R = pl.second.first;
+                S_best = pl.second.second;
+                cached = true;
+            }
+    }
+    for (int S = 1; !cached && S <= 8 && S <= a.nk; S *= 2) {
+        int slots = nsm / S, r = 0;
+        for (int pass = 0; pass < 2; pass++) {
+            r = std::max(8, (int)((total_rows + slots - 1) / std::max(slots, 1)));
+            while (r <= TILE_M && tiles_for(r) > slots) r++;
+            if (r > TILE_M) break;
+            slots = std::min(slots, resident(S, smem_for(r, S, nullptr)));
+            if (slots <= 0) {
+                r = TILE_M + 1;
+                break;
+            }
+        }
+        if (r > TILE_M || tiles_for(r) > slots) continue;
+        const long long ctas = (long long)tiles_for(r) * S;
+        const long long per_sm = (ctas + nsm - 1) / nsm;
+        const long long cost = per_sm * std::max(r, 64) * ((a.nk + S - 1) / S);
         if (best < 0 || cost < best) {
             best = cost;
             R = r;
@@ -452,16 +490,27 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
         while (R < TILE_M && tiles_for(R) > nsm * waves) R++;
         S_best = 1;
     }
+    {
+        std::lock_guard<std::mutex> lock(plan_mu);
+        bool known = false;
+        for (auto &pl : plans) known = known || std::equal(pl.first.begin(), pl.first.end(), key);
+        if (!known) plans.push_back({std::vector<long long>(key, key + 7), {R, S_best}});
+    }
     a.R = R;
     a.splits = S_best;
     a.tile_start[0] = 0;
     for (int i = 0; i < 3; i++) a.tile_start[i + 1] = a.tile_start[i] + (i < n_mat ? (a.rows[i] + R - 1) / R : 0);
     a.n_tiles = a.tile_start[3];
-    a.Bp = std::max(16, (a.B + 15) / 16 * 16);
-    a.stage_bytes = NA * A_TILE_BYTES + a.Bp * BK * 2;
-    a.stages = (int)std::min<size_t>(MAX_STAGES, (SMEM_BUDGET - 1024 - 256) / a.stage_bytes);
-    if (a.stages < 2) a.stages = 2;
-    if ((size_t)a.stages * a.stage_bytes + 1024 + 256 > SMEM_MAX) return Q3_ERR_SHAPE;
+    // A weight tile holds R rows (8-row swizzle atoms). The M = 128 MMA reads 128 rows from the
+    // tile's start; rows past R land in the following shared memory (the next tile, the
+    // activation tiles, or the slack reserved at the end) and produce accumulator rows that the
+    // epilogue never reads.
+    a.a_tile_bytes = (R + 7) / 8 * 8 * BK * 2;
+    a.stage_bytes = a.ksub * (NA * a.a_tile_bytes + a.Bp * BK * 2);
+    int stages = 2;
+    const size_t smem = smem_for(R, a.splits, &stages);
+    a.stages = stages;
+    if (smem > SMEM_MAX) return Q3_ERR_SHAPE;
     uint32_t cols = 32;
     while (cols < (uint32_t)(NA * a.Bp)) cols *= 2;
     a.tmem_cols = cols;
@@ -478,12 +527,6 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
     }
     if (!make_map(&mx, x, a.B, a.K, a.Bp)) return Q3_ERR_ARG;
 
-    // split-K reuses the ring for the fp32 partial tile [128][NA*Bp + 1]
-    if (a.splits > 1 && (size_t)a.stages * a.stage_bytes < (size_t)TILE_M * (NA * a.Bp + 1) * 4) {
-        a.stages = (int)(((size_t)TILE_M * (NA * a.Bp + 1) * 4 + a.stage_bytes - 1) / a.stage_bytes);
-        if ((size_t)a.stages * a.stage_bytes + 1024 + 256 > SMEM_MAX) return Q3_ERR_SHAPE;
-    }
-    const size_t smem = 1024 + (size_t)a.stages * a.stage_bytes + (2 * a.stages + 2) * 8 + 16;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(tc_gemm_kernel<EPI>), smem));
     const int grid = a.splits > 1 ? a.n_tiles * a.splits : std::min(nsm, a.n_tiles);
     Q3_TRY_LAUNCH(launch(tc_gemm_kernel<EPI>, dim3(grid), dim3(TC_THREADS), smem, stream, a.splits, m0, m1, m2, mx, a));

@@ -80,11 +80,7 @@ def test_batched_gemv_residual_matches_per_sequence(batch, rows, cols):
     for b in range(batch):
         q3.gemv_residual_forward(ref_x[b], w, inp[b], rows, cols, tap=ref_tap[b])
     absw = (w.float().abs() @ inp.float().abs().T).T  # [batch, rows] sum of |terms|
-    # the plain batched projection accumulates identically: its output must equal the tap
-    plain = torch.empty_like(tap)
-    _lib.call("q3_gemv_batched", plain.data_ptr(), w.data_ptr(), inp.data_ptr(), batch, rows, cols, stream())
     torch.cuda.synchronize()
-    assert torch.equal(plain, tap), f"tap != plain projection at {int((plain != tap).sum())} elements"
     check_close(tap, ref_tap, absw, "tap")
     expect_x = (x0.float() + tap.float()).bfloat16()
     assert torch.equal(x, expect_x), f"x != bf16(x0 + tap) at {int((x != expect_x).sum())} elements"
