@@ -150,16 +150,20 @@ class Dist:
             self.pg.destroy_process_group()
 
 
-def timed(dist, stream, fn) -> float:
-    """ms of fn() on `stream`, barrier and synchronize on both sides, max over ranks."""
+def timed(dist, stream, fn, name: str) -> float:
+    """ms of fn() on `stream`, barrier and synchronize on both sides, max over ranks. The launches
+    sit in an NVTX range `name`, so a profiler can select the timed region alone
+    (ncu --nvtx --nvtx-include "<name>/")."""
     import torch
     s = torch.cuda.ExternalStream(stream)
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push(name)
     e0.record(s)
     fn()
     e1.record(s)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     dist.barrier()
     return dist.max(e0.elapsed_time(e1))
@@ -209,7 +213,7 @@ def run_mine(args) -> dict | None:
     torch.cuda.synchronize()
 
     with ClockSampler(torch.cuda.current_device()) as clk:
-        ms = timed(dist, stream.cuda_stream, lambda: eng.step(K))
+        ms = timed(dist, stream.cuda_stream, lambda: eng.step(K), "decode_steps")
         # e2e: the per-token host protocol, continuing from the device loop's state
         toks = eng.sample_argmax()
         pos0 = KV_PREFILL + W + K
@@ -218,7 +222,7 @@ def run_mine(args) -> dict | None:
             for i in range(K):
                 eng.forward(t, [pos0 + i] * B)
                 t = eng.sample_argmax()
-        ms_e2e = timed(dist, stream.cuda_stream, e2e)
+        ms_e2e = timed(dist, stream.cuda_stream, e2e, "decode_e2e")
     clocks = clk.summary()
     if q3.device_error(stream.cuda_stream) != 0:
         raise SystemExit("device error flags set during the benchmark")
@@ -276,6 +280,7 @@ def kernel_roofline(eng, stream, hbm_peak, measured) -> dict:
     out = torch.empty_like(q)
     scale = 1.0 / s.head_dim ** 0.5
     layer_stride = B * eng.max_seq * kvd * 2  # bytes between layers' caches
+    hd = s.head_dim  # the engine's caches are head-major: [B][n_kv][max_seq][head_dim] per layer
     reps = 20
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -285,7 +290,8 @@ def kernel_roofline(eng, stream, hbm_peak, measured) -> dict:
             ev0.record(ts)
         layer = i % s.num_hidden_layers  # a different layer's cache each launch: no L2 reuse
         _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), buf.key_cache + layer * layer_stride,
-                  buf.value_cache + layer * layer_stride, eng.max_seq * kvd, scratch.data_ptr(), pos.data_ptr(), B,
+                  buf.value_cache + layer * layer_stride, eng.max_seq * kvd, hd, eng.max_seq * hd,
+                  scratch.data_ptr(), pos.data_ptr(), B,
                   s.num_attention_heads, s.num_key_value_heads, s.head_dim, eng.max_seq, scale, stream.cuda_stream)
     ev1.record(ts)
     torch.cuda.synchronize()

@@ -116,9 +116,13 @@ int q3_sample_forward(int *out, const q3_bf16 *x, int n, float inv_temp, float u
 /* ---------------------------------------------------------------------------------------
  * Batched launchers: `batch` independent decode sequences. The reference has no batch
  * dimension; per sequence each computes what the reference launcher computes for it.
- * Activations are [batch, dim] row-major. Sequence b's KV cache rows start at
- * cache + b * cache_seq_stride (elements); token ids and positions are per sequence in
- * device memory. Projections with batch 1 run the bit-exact batch-1 kernels; batch >= 2 runs
+ * Activations are [batch, dim] row-major. A KV cache is addressed by three element strides:
+ * the row of sequence b, position t, kv head h starts at
+ * cache + b*cache_seq_stride + t*cache_pos_stride + h*cache_head_stride. The reference's layout
+ * (one layer's [max_seq][n_kv_heads * head_dim]) is pos = n_kv_heads*head_dim, head = head_dim;
+ * head-major caches ([n_kv_heads][max_seq][head_dim] per sequence: pos = head_dim,
+ * head = max_seq*head_dim) keep each head's positions contiguous, which attention reads in
+ * longer runs. Token ids and positions are per sequence in device memory. Projections with batch 1 run the bit-exact batch-1 kernels; batch >= 2 runs
  * the tcgen05 tensor-core GEMM (fp32 sums in the tensor core's order).
  * ------------------------------------------------------------------------------------- */
 
@@ -145,9 +149,9 @@ int q3_gate_up_batched(q3_bf16 *act, const q3_bf16 *w_gate, const q3_bf16 *w_up,
  * device error bit 2 and skip that sequence. */
 int q3_qk_norm_rope_batched(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_bf16 *q_norm_w,
                             const q3_bf16 *k_norm_w, q3_bf16 *key_cache, q3_bf16 *value_cache,
-                            long long cache_seq_stride, const int *d_pos, int batch, int n_heads, int n_kv_heads,
-                            int head_dim, int max_seq, float eps, float theta, q3_bf16 *q_tap, q3_bf16 *k_tap,
-                            void *stream);
+                            long long cache_seq_stride, long long cache_pos_stride, long long cache_head_stride,
+                            const int *d_pos, int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                            float eps, float theta, q3_bf16 *q_tap, q3_bf16 *k_tap, void *stream);
 
 /* Bytes of scratch q3_attention_batched needs (0 for unsupported shapes: head_dim above 256 or
  * a group size n_heads / n_kv_heads other than 1, 2, 4 or 8). */
@@ -157,8 +161,9 @@ size_t q3_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int he
  * points for scores and probabilities; `scratch` (size from q3_attention_scratch_bytes) needs no
  * initialization. Calls sharing a scratch buffer must not overlap on the GPU. */
 int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache, const q3_bf16 *value_cache,
-                         long long cache_seq_stride, void *scratch, const int *d_pos, int batch, int n_heads,
-                         int n_kv_heads, int head_dim, int max_seq, float scale, void *stream);
+                         long long cache_seq_stride, long long cache_pos_stride, long long cache_head_stride,
+                         void *scratch, const int *d_pos, int batch, int n_heads, int n_kv_heads, int head_dim,
+                         int max_seq, float scale, void *stream);
 
 /* out[b] = argmax of x[b][0..n) with argmax_forward's tie and NaN rules. */
 int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream);
@@ -206,7 +211,7 @@ typedef struct q3_engine q3_engine;
 typedef struct q3_engine_buffers {
     q3_bf16 *x;            /* [batch, hidden] residual stream after the last step */
     q3_bf16 *logits;       /* [batch, vocab] */
-    q3_bf16 *key_cache;    /* [n_layers][batch][max_seq][n_kv_heads * head_dim] */
+    q3_bf16 *key_cache;    /* [n_layers][batch][n_kv_heads][max_seq][head_dim] (head-major) */
     q3_bf16 *value_cache;
     int *next_token;       /* [batch] read by the next step's embedding */
     int *pos;              /* [batch] position the next step writes and attends up to */

@@ -44,9 +44,9 @@ SIGNATURES: dict[str, list] = {
     "q3_gemv_residual_batched": [_P, _P, _P, _I, _I, _I, _P, _P],
     "q3_qkv_batched": [_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _P],
     "q3_gate_up_batched": [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P],
-    "q3_qk_norm_rope_batched": [_P, _P, _P, _P, _P, _P, _P, _LL, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P],
+    "q3_qk_norm_rope_batched": [_P, _P, _P, _P, _P, _P, _P, _LL, _LL, _LL, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P],
     "q3_attention_scratch_bytes": [_I, _I, _I, _I, _I],
-    "q3_attention_batched": [_P, _P, _P, _P, _LL, _P, _P, _I, _I, _I, _I, _I, _F, _P],
+    "q3_attention_batched": [_P, _P, _P, _P, _LL, _LL, _LL, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "q3_argmax_batched": [_P, _P, _I, _I, _P],
     "q3_fill_normal_bf16": [_P, _LL, ctypes.c_ulonglong, _F, _F, _P],
     "q3_weight_bytes_per_step": [_P],

@@ -20,13 +20,13 @@ int embedding(bf16 *out, const bf16 *table, const int *tokens, int n_rows, int h
 int rmsnorm(bf16 *out, const bf16 *in, const bf16 *weight, int rows, int dim, float eps, cudaStream_t s);
 int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf16 *k_norm_w,
                  bf16 *key_cache, bf16 *value_cache, const int *pos, int n_rows, long long q_stride,
-                 long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
+                 long long kv_stride, KvLayout kv, int n_heads, int n_kv_heads, int head_dim,
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
 int sample(int *out, const bf16 *x, int n, float inv_temp, float u, cudaStream_t s);
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              const int *pos, int n_rows, long long q_stride, KvLayout kv, int n_heads, int n_kv_heads,
               int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 unsigned take_error_gemv();
 unsigned take_error_decode();
@@ -179,8 +179,9 @@ int q3_qk_norm_rope_forward(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_b
                             float theta, q3_bf16 *q_tap, q3_bf16 *k_tap, void *stream) {
     DEVICE_OR_RETURN();
     const long long qd = (long long)n_heads * head_dim, kvd = (long long)n_kv_heads * head_dim;
+    const q3::KvLayout kv = {0, kvd, head_dim};  // the reference's [max_seq][n_kv * head_dim] cache
     return q3::qk_norm_rope(B(q), B(k), CB(v), CB(q_norm_w), CB(k_norm_w), B(key_cache), B(value_cache),
-                            d_pos, 1, qd, kvd, 0, n_heads, n_kv_heads, head_dim, 0, eps, theta, B(q_tap),
+                            d_pos, 1, qd, kvd, kv, n_heads, n_kv_heads, head_dim, 0, eps, theta, B(q_tap),
                             B(k_tap), S(stream));
 }
 
@@ -188,8 +189,9 @@ int q3_attention_forward(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
                          const q3_bf16 *value_cache, float *att, int n_heads, int n_kv_heads, int head_dim,
                          const int *d_pos, int max_seq, float scale, void *stream) {
     DEVICE_OR_RETURN();
+    const q3::KvLayout kv = {0, (long long)n_kv_heads * head_dim, head_dim};
     return q3::attention(B(out), CB(q), CB(key_cache), CB(value_cache), att, max_seq, d_pos, 1,
-                         (long long)n_heads * head_dim, 0, n_heads, n_kv_heads, head_dim, max_seq, scale,
+                         (long long)n_heads * head_dim, kv, n_heads, n_kv_heads, head_dim, max_seq, scale,
                          nullptr, S(stream));
 }
 

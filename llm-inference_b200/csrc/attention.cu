@@ -55,13 +55,14 @@ constexpr int STATS_SMEM = 160 * 1024;
 
 struct AttnArgs {
     const bf16 *q;        // sequence b: q + b*q_stride, heads concatenated
-    const bf16 *kc, *vc;  // sequence b: kc + b*cache_stride, rows [max_seq][kv_dim]
+    const bf16 *kc, *vc;  // row (b, t, kv head h) at kc + b*kv.seq + t*kv.pos + h*kv.head
     bf16 *out;            // like q
     float *scores;        // [B][n_heads][ld]
     float *stats;         // split mode: [B][n_heads][2] (max, sum of exp)
     float *partial;       // split mode: [B][n_heads][max_chunks][head_dim]
     const int *pos;       // [B]
-    long long q_stride, cache_stride;
+    long long q_stride;
+    KvLayout kv;
     int ld;               // row stride of scores (>= max_seq)
     int B, n_heads, n_kv, head_dim, kv_dim, max_seq;
     int chunk_b;          // positions per pv item
@@ -111,6 +112,31 @@ __device__ __forceinline__ Item find_item(const AttnArgs &a, const int *prefix, 
     Item it;
     int b = 0;
     while (prefix[b + 1] <= item) b++;
+    it.b = b;
+    it.len = seq_len(a, b);
+    it.nc = (it.len + chunk - 1) / chunk;
+    const int r = item - prefix[b];
+    it.kvh = r / it.nc;
+    it.c = r - it.kvh * it.nc;
+    return it;
+}
+
+// Sequence whose items contain `item` (prefix[B] > item): the largest b with prefix[b] <= item,
+// which skips sequences without items.
+__device__ __forceinline__ int first_seq(const int *prefix, int B, int item) {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) / 2;
+        if (prefix[mid] <= item) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
+
+// find_item for increasing items: `b` is the caller's cursor (start it at first_seq).
+__device__ __forceinline__ Item item_at(const AttnArgs &a, const int *prefix, int chunk, int item, int &b) {
+    while (prefix[b + 1] <= item) b++;
+    Item it;
     it.b = b;
     it.len = seq_len(a, b);
     it.nc = (it.len + chunk - 1) / chunk;
@@ -213,11 +239,11 @@ __global__ void __launch_bounds__(SC_THREADS) attn_scores_kernel(const __grid_co
         const Item it = find_item(a, prefix, a.sc_chunk, item);
         const int t0 = it.c * a.sc_chunk;
         const int rows = min(a.sc_chunk, it.len - t0);
-        const bf16 *src = a.kc + (size_t)it.b * a.cache_stride + (size_t)t0 * a.kv_dim + (size_t)it.kvh * hd;
+        const bf16 *src = a.kc + (size_t)it.b * a.kv.seq + (size_t)t0 * a.kv.pos + (size_t)it.kvh * a.kv.head;
         bf16 *dst = ktiles + (size_t)stage * tile_elems;
         for (int j = tid; j < rows * cpr; j += SC_THREADS) {
             const int r = j / cpr, ch = j - r * cpr;
-            cp_async16(dst + r * row_elems + ch * 8, src + (size_t)r * a.kv_dim + ch * 8);
+            cp_async16(dst + r * row_elems + ch * 8, src + (size_t)r * a.kv.pos + ch * 8);
         }
     };
 
@@ -325,7 +351,7 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
         const int t1 = min(t0 + chunk, it.len);
         const int n_tiles = (t1 - t0 + VT - 1) / VT;
         const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
-        const bf16 *vsrc = a.vc + (size_t)it.b * a.cache_stride + (size_t)it.kvh * hd;
+        const bf16 *vsrc = a.vc + (size_t)it.b * a.kv.seq + (size_t)it.kvh * a.kv.head;
 
         auto issue = [&](int tile) {
             const int st = tile % V_STAGES;
@@ -334,7 +360,7 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
             bf16 *dst = vtile + st * VT * hd;
             for (int j = tid; j < rows * cpr; j += THREADS) {
                 const int r = j / cpr, ch = j - r * cpr;
-                cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv_dim + ch * 8);
+                cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv.pos + ch * 8);
             }
 #pragma unroll
             for (int h = 0; h < NREP; h++) stage_scores(s_tile + (st * NREP + h) * VT, sc + (size_t)h * a.ld + tt0, rows);
@@ -425,11 +451,14 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 constexpr int TC_TILE = 128;        // positions per item = MMA M
 constexpr int TC_N = 16;            // MMA N: query heads of the group, padded
 constexpr int TC_STAGES = 4;
+constexpr int TC_ACC = 4;           // TMEM accumulators (TC_N columns each)
 constexpr int TC_THREADS = 192;     // producer warp, MMA warp, 4 epilogue warps
 
 struct ScoreTcPlan {
     int halves;         // head_dim / 64
-    int k_rows_per_seq; // rows of the K map per sequence (cache_stride / kv_dim)
+    int k_rows_per_seq; // rows of the K map per sequence (kv.seq / kv.pos)
+    int k_rows_per_head;  // head-major caches: rows per kv head (kv.head / kv.pos), else 0
+    int k_cols_per_head;  // heads within a row: columns per kv head (kv.head), else 0
     int stage_bytes;
     uint32_t idesc;
 };
@@ -444,9 +473,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int qbytes = TC_N * 128;     // one 64-dim half of the query rows
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)TC_STAGES * pl.stage_bytes);
     uint64_t *empty = full + TC_STAGES;
-    uint64_t *acc_full = empty + TC_STAGES;    // [2]
-    uint64_t *acc_empty = acc_full + 2;        // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
+    uint64_t *acc_full = empty + TC_STAGES;    // [TC_ACC]
+    uint64_t *acc_empty = acc_full + TC_ACC;   // [TC_ACC]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + TC_ACC);
     int *prefix = reinterpret_cast<int *>(tmem_slot + 4);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -455,7 +484,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], 1);
         }
-        for (int i = 0; i < 2; i++) {
+        for (int i = 0; i < TC_ACC; i++) {
             mbar_init(&acc_full[i], 1);
             mbar_init(&acc_empty[i], 128);
         }
@@ -465,7 +494,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(32)
+                     "r"(TC_ACC * TC_N)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -480,6 +509,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     const int n = i1 - i0;
+    int cur = n > 0 ? first_seq(prefix, a.B, i0) : 0;  // this thread's sequence cursor
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer
@@ -487,13 +517,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (; k < n; k++) {
             const int st = k % TC_STAGES;
             if (k >= TC_STAGES && !mbar_wait(&empty[st], ((k / TC_STAGES) - 1) & 1, &g_dev_error)) break;
-            const Item it = find_item(a, prefix, TC_TILE, i0 + k);
+            const Item it = item_at(a, prefix, TC_TILE, i0 + k, cur);
             unsigned char *base = smem + (size_t)st * pl.stage_bytes;
             mbar_arrive_expect_tx(&full[st], (uint32_t)pl.halves * (kbytes + qbytes));
-            const int krow = it.b * pl.k_rows_per_seq + it.c * TC_TILE;
+            const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * TC_TILE;
             const int qrow = it.b * a.n_heads + it.kvh * NREP;
             for (int h = 0; h < pl.halves; h++) {
-                tma_load_2d(base + h * kbytes, &tmK, it.kvh * a.head_dim + h * TMA_BK, krow, &full[st]);
+                tma_load_2d(base + h * kbytes, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow, &full[st]);
                 tma_load_2d(base + pl.halves * kbytes + h * qbytes, &tmQ, h * TMA_BK, qrow, &full[st]);
             }
         }
@@ -501,8 +531,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer: 16 head dims per instruction
         for (int k = 0; k < n; k++) {
-            const int st = k % TC_STAGES, buf = k & 1;
-            if (k >= 2 && !mbar_wait(&acc_empty[buf], ((k >> 1) - 1) & 1, &g_dev_error)) break;
+            const int st = k % TC_STAGES, buf = k % TC_ACC;
+            if (k >= TC_ACC && !mbar_wait(&acc_empty[buf], ((k / TC_ACC) - 1) & 1, &g_dev_error)) break;
             if (!mbar_wait(&full[st], (k / TC_STAGES) & 1, &g_dev_error)) break;
             tc_fence_after();
             const uint32_t kb = smem_u32(smem + (size_t)st * pl.stage_bytes);
@@ -521,20 +551,232 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int row = quarter * 32 + lane;
         const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
         for (int k = 0; k < n; k++) {
-            const int buf = k & 1;
-            if (!mbar_wait(&acc_full[buf], (k >> 1) & 1, &g_dev_error)) break;
+            const int buf = k % TC_ACC;
+            if (!mbar_wait(&acc_full[buf], (k / TC_ACC) & 1, &g_dev_error)) break;
             tc_fence_after();
             float acc[8];
             tmem_ld8(lane_addr + buf * TC_N, acc);
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(&acc_empty[buf]);
-            const Item it = find_item(a, prefix, TC_TILE, i0 + k);
+            const Item it = item_at(a, prefix, TC_TILE, i0 + k, cur);
             const int t = it.c * TC_TILE + row;
             if (t < it.len) {
                 float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld + t;
 #pragma unroll
                 for (int h = 0; h < NREP; h++) sc[(size_t)h * a.ld] = round_bf16(round_bf16(acc[h]) * a.scale);
+            }
+        }
+    }
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_ACC * TC_N)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ pv on tcgen05 (split mode)
+// One item = (b, kv head, chunk of positions); per 128-position tile the MMA computes
+// D[head_dim x 16] += V_tile^T[head_dim x 128] . P^T[128 x 16] into a TMEM accumulator.
+//   A = V tile, loaded by TMA as two 64-dim halves of [128 positions][64 dims] (128-byte swizzle):
+//       MN-major (dims contiguous), LBO = 16 KB between the halves, SBO = 1 KB per 8 positions.
+//   B = P, [16 rows][128 positions] bf16 written by the p warps in the K-major 128-byte swizzle
+//       layout: row h holds p = round_bf16(expf(s - max) / sum) of query head h of the group
+//       (src/kernels.cu:472-474), rows NREP..15 are zero, as are positions past the sequence.
+// p and v are bf16 and the accumulator fp32, so every product is exact; only the order of the
+// fp32 additions differs from a serial chain. V rows past the end of the sequence are zeroed in
+// shared memory before the MMA (the cache there may hold anything, and 0 * NaN is NaN).
+constexpr int PV_TILE = 128;
+constexpr int PV_STAGES = 4;
+constexpr int PV_ACC = 2;
+constexpr int PV_V_BYTES = PV_TILE * 128;      // one 64-dim half of a V tile
+constexpr int PV_P_OFF = 2 * PV_V_BYTES;       // P: 2 swizzle atoms of 16 rows x 128 B
+constexpr int PV_S_OFF = PV_P_OFF + 2 * 16 * 128;
+constexpr int PV_STAGE_BYTES = PV_S_OFF + 8 * PV_TILE * 4;  // scores of up to 8 heads
+
+struct PvTcPlan {
+    int k_rows_per_seq, k_rows_per_head, k_cols_per_head;
+    uint32_t idesc;
+};
+
+template <int NREP>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    attn_pv_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a,
+                      const __grid_constant__ PvTcPlan pl) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)PV_STAGES * PV_STAGE_BYTES);
+    uint64_t *pfull = full + PV_STAGES;
+    uint64_t *empty = pfull + PV_STAGES;
+    uint64_t *acc_full = empty + PV_STAGES;
+    uint64_t *acc_empty = acc_full + PV_ACC;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + PV_ACC);
+    int *prefix = reinterpret_cast<int *>(tmem_slot + 4);
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int chunk = a.chunk_b;  // a multiple of PV_TILE
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < PV_STAGES; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&pfull[i], 128);
+            mbar_init(&empty[i], 1);
+        }
+        for (int i = 0; i < PV_ACC; i++) {
+            mbar_init(&acc_full[i], 1);
+            mbar_init(&acc_empty[i], 128);
+        }
+        fence_barrier_init();
+        prefetch_tmap(&tmV);
+    }
+    if (warp >= 2) {  // zero the padding rows NREP..15 of every stage's P once
+        const int t = threadIdx.x - 64;
+        for (int j = t; j < PV_STAGES * 2 * 16 * 8; j += 128) {  // 16-byte units
+            const int st = j / 256, r = j % 256, atom = r / 128, row = (r % 128) / 8, c = r % 8;
+            if (row >= NREP)
+                *reinterpret_cast<uint4 *>(smem + (size_t)st * PV_STAGE_BYTES + PV_P_OFF + atom * 2048 + row * 128 + c * 16) =
+                    make_uint4(0, 0, 0, 0);
+        }
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(32)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    pdl_trigger();
+    pdl_wait();  // positions, scores and statistics come from the previous kernels
+    const int total = build_prefix(a, chunk, prefix);
+    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    int cur = i1 > i0 ? first_seq(prefix, a.B, i0) : 0;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- producer: V tile halves by TMA, the group's scores by bulk copy
+        int k = 0;
+        bool ok = true;
+        for (int item = i0; item < i1 && ok; item++) {
+            const Item it = item_at(a, prefix, chunk, item, cur);
+            const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
+            const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
+            const int row0 = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head;
+            for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
+                const int st = k % PV_STAGES;
+                if (k >= PV_STAGES && !mbar_wait(&empty[st], ((k / PV_STAGES) - 1) & 1, &g_dev_error)) {
+                    ok = false;
+                    break;
+                }
+                const int rows = min(PV_TILE, t1 - tt);
+                const uint32_t sbytes = (uint32_t)((rows + 3) / 4) * 16;  // within ld: ld is a multiple of 4
+                unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + NREP * sbytes);
+                tma_load_2d(base, &tmV, it.kvh * pl.k_cols_per_head, row0 + tt, &full[st]);
+                tma_load_2d(base + PV_V_BYTES, &tmV, it.kvh * pl.k_cols_per_head + TMA_BK, row0 + tt, &full[st]);
+#pragma unroll
+                for (int h = 0; h < NREP; h++)
+                    bulk_g2s(base + PV_S_OFF + h * PV_TILE * 4, sc + (size_t)h * a.ld + tt, sbytes, &full[st]);
+            }
+        }
+        // drain: every issued copy lands before the CTA exits
+        for (int j = max(0, k - PV_STAGES); j < k; j++) mbar_wait(&full[j % PV_STAGES], (j / PV_STAGES) & 1, &g_dev_error);
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer
+        int k = 0, n_items = 0;
+        bool ok = true;
+        for (int item = i0; item < i1 && ok; item++, n_items++) {
+            const Item it = item_at(a, prefix, chunk, item, cur);
+            const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
+            const int buf = n_items % PV_ACC;
+            if (n_items >= PV_ACC && !mbar_wait(&acc_empty[buf], ((n_items / PV_ACC) - 1) & 1, &g_dev_error)) break;
+            const uint32_t d_tmem = tmem_base + buf * 16;
+            for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
+                const int st = k % PV_STAGES;
+                if (!mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error) ||
+                    !mbar_wait(&pfull[st], (k / PV_STAGES) & 1, &g_dev_error)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t vb = smem_u32(smem + (size_t)st * PV_STAGE_BYTES);
+                const uint32_t pb = vb + PV_P_OFF;
+#pragma unroll
+                for (int kk = 0; kk < PV_TILE / 16; kk++) {
+                    const uint64_t ad = smem_desc_sw128(vb + kk * 16 * 128, PV_V_BYTES, 1024);
+                    const uint64_t bd = smem_desc_sw128(pb + (kk / 4) * 2048 + (kk % 4) * 32, 16, 1024);
+                    mma_bf16(d_tmem, ad, bd, pl.idesc, (tt > t0 || kk > 0) ? 1u : 0u);
+                }
+                mma_commit(&empty[st]);
+            }
+            if (ok) mma_commit(&acc_full[buf]);
+        }
+    } else if (warp >= 2) {
+        // ---------------- p warps: one position per thread; then the item's epilogue
+        const int t = threadIdx.x - 64;
+        const int quarter = warp % 4;
+        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+        const int d = quarter * 32 + lane;  // accumulator row = head dim
+        int k = 0, n_items = 0;
+        bool ok = true;
+        for (int item = i0; item < i1 && ok; item++, n_items++) {
+            const Item it = item_at(a, prefix, chunk, item, cur);
+            const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
+            float m[NREP], sum[NREP];
+#pragma unroll
+            for (int h = 0; h < NREP; h++) {
+                const float *stp = a.stats + ((size_t)it.b * a.n_heads + it.kvh * NREP + h) * 2;
+                m[h] = __ldcg(stp);
+                sum[h] = __ldcg(stp + 1);
+            }
+            for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
+                const int st = k % PV_STAGES;
+                if (!mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
+                const int rows = min(PV_TILE, t1 - tt);
+                const float *s_st = reinterpret_cast<const float *>(base + PV_S_OFF);
+                unsigned char *prow = base + PV_P_OFF + (t / 64) * 2048 + (t % 8) * 2;
+                const int c16 = (t % 64) / 8;
+#pragma unroll
+                for (int h = 0; h < NREP; h++) {
+                    const float p = t < rows ? round_bf16(expf(s_st[h * PV_TILE + t] - m[h]) / sum[h]) : 0.0f;
+                    *reinterpret_cast<bf16 *>(prow + h * 128 + ((c16 ^ (h & 7)) << 4)) = __float2bfloat16(p);
+                }
+                if (t >= rows) {  // V rows past the sequence: zero both halves of row t
+                    uint4 *v0 = reinterpret_cast<uint4 *>(base + t * 128);
+                    uint4 *v1 = reinterpret_cast<uint4 *>(base + PV_V_BYTES + t * 128);
+#pragma unroll
+                    for (int c = 0; c < 8; c++) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async();
+                mbar_arrive(&pfull[st]);
+            }
+            if (!ok) break;
+            const int buf = n_items % PV_ACC;
+            if (!mbar_wait(&acc_full[buf], (n_items / PV_ACC) & 1, &g_dev_error)) break;
+            tc_fence_after();
+            float acc[8];
+            tmem_ld8(lane_addr + buf * 16, acc);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+            if (d < a.head_dim) {
+                if (it.nc == 1) {
+                    bf16 *o = a.out + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * a.head_dim + d;
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) o[(size_t)h * a.head_dim] = __float2bfloat16(acc[h]);
+                } else {
+                    float *part = a.partial + ((size_t)it.b * a.n_heads + it.kvh * NREP) * a.max_chunks * a.head_dim;
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) part[((size_t)h * a.max_chunks + it.c) * a.head_dim + d] = acc[h];
+                }
             }
         }
     }
@@ -580,7 +822,7 @@ __global__ void __launch_bounds__(THREADS) attn_pv_vec_kernel(const __grid_const
         const int t1 = min(t0 + chunk, it.len);
         const int n_tiles = (t1 - t0 + VT - 1) / VT;
         const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
-        const bf16 *vsrc = a.vc + (size_t)it.b * a.cache_stride + (size_t)it.kvh * hd;
+        const bf16 *vsrc = a.vc + (size_t)it.b * a.kv.seq + (size_t)it.kvh * a.kv.head;
         auto issue = [&](int tile) {
             const int st = tile % V_STAGES;
             const int tt0 = t0 + tile * VT;
@@ -588,7 +830,7 @@ __global__ void __launch_bounds__(THREADS) attn_pv_vec_kernel(const __grid_const
             bf16 *dst = vtile + st * VT * hd;
             for (int j = tid; j < rows * cpr; j += THREADS) {
                 const int r = j / cpr, ch = j - r * cpr;
-                cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv_dim + ch * 8);
+                cp_async16(dst + r * hd + ch * 8, vsrc + (size_t)(tt0 + r) * a.kv.pos + ch * 8);
             }
 #pragma unroll
             for (int h = 0; h < NREP; h++) stage_scores(s_tile + (st * NREP + h) * VT, sc + (size_t)h * a.ld + tt0, rows);
@@ -692,12 +934,14 @@ template <int NREP>
 int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     ScoreTcPlan pl;
     pl.halves = a.head_dim / TMA_BK;
-    pl.k_rows_per_seq = (int)(a.cache_stride / a.kv_dim);
+    pl.k_rows_per_seq = (int)(a.kv.seq / a.kv.pos);
+    pl.k_rows_per_head = a.kv.head >= a.kv.pos ? (int)(a.kv.head / a.kv.pos) : 0;
+    pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
     pl.stage_bytes = pl.halves * (TC_TILE * 128 + TC_N * 128);
     // kind::f16: fp32 accumulate, bf16 A and B, both K-major, N = 16, M = 128
     pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_TILE >> 4) << 24);
     CUtensorMap mk, mq;
-    if (!make_map_strided(&mk, a.kc, (long long)a.B * pl.k_rows_per_seq, a.kv_dim, a.kv_dim, TC_TILE)) return Q3_ERR_ARG;
+    if (!make_map_strided(&mk, a.kc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, TC_TILE)) return Q3_ERR_ARG;
     if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TC_N)) return Q3_ERR_ARG;
     const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)(a.B + 1) * 4;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_tc_kernel<NREP>), smem));
@@ -707,12 +951,34 @@ int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     return Q3_OK;
 }
 
+template <int NREP>
+int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
+    PvTcPlan pl;
+    pl.k_rows_per_seq = (int)(a.kv.seq / a.kv.pos);
+    pl.k_rows_per_head = a.kv.head >= a.kv.pos ? (int)(a.kv.head / a.kv.pos) : 0;
+    pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
+    // kind::f16: fp32 accumulate, bf16 A (MN-major) and B (K-major), N = 16, M = 128
+    pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) |
+               ((uint32_t)(128 >> 4) << 24);
+    CUtensorMap mv;
+    if (!make_map_strided(&mv, a.vc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
+    const size_t smem = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)(a.B + 1) * 4;
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
+    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
+    const int grid = (int)std::min<long long>(max_items, num_sms());
+    Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP>, dim3(grid), dim3(TC_THREADS), smem, s, 1, mv, a, pl));
+    return Q3_OK;
+}
+
 // The tensor-core scores need whole 64-dim halves, contiguous per-sequence caches in kv_dim rows,
 // and a packed q; the vectorized pv needs an even head_dim that splits 128 threads into groups.
 bool split_fast_path(const AttnArgs &a) {
-    return a.head_dim % TMA_BK == 0 && a.head_dim <= 256 && a.cache_stride % a.kv_dim == 0 &&
+    const KvLayout &kv = a.kv;
+    const bool heads_in_row = kv.head < kv.pos;  // reference layout
+    return a.head_dim % TMA_BK == 0 && a.head_dim <= 256 && kv.pos > 0 && kv.seq % kv.pos == 0 &&
+           (heads_in_row ? kv.head % 8 == 0 : kv.head % kv.pos == 0) && kv.pos % 8 == 0 &&
            a.q_stride == (long long)a.n_heads * a.head_dim && 128 % (a.head_dim / 2) == 0 &&
-           (a.cache_stride / a.kv_dim) * (long long)a.B < (1LL << 31);
+           (kv.seq / kv.pos) * (long long)a.B < (1LL << 31);
 }
 
 template <int NREP>
@@ -725,6 +991,12 @@ int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
         if (st != Q3_OK) return st;
         Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), STATS_SMEM));
         Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), (size_t)STATS_SMEM, s, 1, a));
+        if (a.head_dim == 128 && a.chunk_b % PV_TILE == 0) {  // P.V on the tensor cores
+            st = launch_pv_tc<NREP>(a, s);
+            if (st != Q3_OK) return st;
+            Q3_TRY_LAUNCH(launch(attn_combine_kernel, dim3(a.n_heads, a.B), dim3(128), 0, s, 1, a));
+            return Q3_OK;
+        }
         const int G = THREADS / (a.head_dim / 2);
         const size_t pv_smem = (size_t)V_STAGES * VT * a.head_dim * 2 + (size_t)V_STAGES * NREP * VT * 4 +
                                (size_t)VT * NREP * 4 + (size_t)G * NREP * a.head_dim * 4 + prefix_bytes;
@@ -789,14 +1061,14 @@ int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int 
 // mode when split == nullptr; otherwise `split` holds the split-mode scratch (stats, partial,
 // chunk_b, max_chunks; the counters are unused).
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              const int *pos, int n_rows, long long q_stride, KvLayout kv, int n_heads, int n_kv_heads,
               int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s) {
     if (!out || !q || !key_cache || !value_cache || !scores || !pos) return Q3_ERR_ARG;
     int st = attention_check(n_heads, n_kv_heads, head_dim, max_seq, n_rows);
     if (st != Q3_OK) return st;
-    if (ld < max_seq) return Q3_ERR_SHAPE;
+    if (ld < max_seq || kv.pos <= 0 || kv.seq < 0 || kv.head < 0) return Q3_ERR_SHAPE;
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    if (!al(key_cache) || !al(value_cache) || (cache_stride * 2) % 16 != 0) return Q3_ERR_ALIGN;
+    if (!al(key_cache) || !al(value_cache) || kv.seq % 8 || kv.pos % 8 || kv.head % 8) return Q3_ERR_ALIGN;
     AttnArgs a = {};
     a.q = q;
     a.kc = key_cache;
@@ -806,7 +1078,7 @@ int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value
     a.ld = ld;
     a.pos = pos;
     a.q_stride = q_stride;
-    a.cache_stride = cache_stride;
+    a.kv = kv;
     a.B = n_rows;
     a.n_heads = n_heads;
     a.n_kv = n_kv_heads;

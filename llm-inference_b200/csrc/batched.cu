@@ -28,12 +28,12 @@ int embedding(bf16 *out, const bf16 *table, const int *tokens, int n_rows, int h
               cudaStream_t s);
 int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf16 *k_norm_w,
                  bf16 *key_cache, bf16 *value_cache, const int *pos, int n_rows, long long q_stride,
-                 long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
+                 long long kv_stride, KvLayout kv, int n_heads, int n_kv_heads, int head_dim,
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              const int *pos, int n_rows, long long q_stride, KvLayout kv, int n_heads, int n_kv_heads,
               int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
 
@@ -175,14 +175,15 @@ int q3_gate_up_batched(q3_bf16 *act, const q3_bf16 *w_gate, const q3_bf16 *w_up,
 
 int q3_qk_norm_rope_batched(q3_bf16 *q, q3_bf16 *k, const q3_bf16 *v, const q3_bf16 *q_norm_w,
                             const q3_bf16 *k_norm_w, q3_bf16 *key_cache, q3_bf16 *value_cache,
-                            long long cache_seq_stride, const int *d_pos, int batch, int n_heads, int n_kv_heads,
-                            int head_dim, int max_seq, float eps, float theta, q3_bf16 *q_tap, q3_bf16 *k_tap,
-                            void *stream) {
+                            long long cache_seq_stride, long long cache_pos_stride, long long cache_head_stride,
+                            const int *d_pos, int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                            float eps, float theta, q3_bf16 *q_tap, q3_bf16 *k_tap, void *stream) {
     DEVICE_OR_RETURN();
-    if (max_seq <= 0) return Q3_ERR_SHAPE;
+    if (max_seq <= 0 || cache_pos_stride <= 0) return Q3_ERR_SHAPE;
+    const KvLayout kv = {cache_seq_stride, cache_pos_stride, cache_head_stride};
     return qk_norm_rope(B(q), B(k), CB(v), CB(q_norm_w), CB(k_norm_w), B(key_cache), B(value_cache), d_pos, batch,
-                        (long long)n_heads * head_dim, (long long)n_kv_heads * head_dim, cache_seq_stride, n_heads,
-                        n_kv_heads, head_dim, max_seq, eps, theta, B(q_tap), B(k_tap), S(stream));
+                        (long long)n_heads * head_dim, (long long)n_kv_heads * head_dim, kv, n_heads, n_kv_heads,
+                        head_dim, max_seq, eps, theta, B(q_tap), B(k_tap), S(stream));
 }
 
 size_t q3_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq) {
@@ -191,8 +192,9 @@ size_t q3_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int he
 }
 
 int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache, const q3_bf16 *value_cache,
-                         long long cache_seq_stride, void *scratch, const int *d_pos, int batch, int n_heads,
-                         int n_kv_heads, int head_dim, int max_seq, float scale, void *stream) {
+                         long long cache_seq_stride, long long cache_pos_stride, long long cache_head_stride,
+                         void *scratch, const int *d_pos, int batch, int n_heads, int n_kv_heads, int head_dim,
+                         int max_seq, float scale, void *stream) {
     DEVICE_OR_RETURN();
     if (!scratch) return Q3_ERR_ARG;
     int st = attention_check(n_heads, n_kv_heads, head_dim, max_seq, batch);
@@ -200,9 +202,10 @@ int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
     AttnSplit sp;
     float *scores = nullptr;
     attention_scratch_layout(batch, n_heads, n_kv_heads, head_dim, max_seq, &sp, &scores, scratch);
+    const KvLayout kv = {cache_seq_stride, cache_pos_stride, cache_head_stride};
     return attention(B(out), CB(q), CB(key_cache), CB(value_cache), scores, score_ld(max_seq), d_pos, batch,
-                     (long long)n_heads * head_dim, cache_seq_stride, n_heads, n_kv_heads, head_dim, max_seq, scale,
-                     &sp, S(stream));
+                     (long long)n_heads * head_dim, kv, n_heads, n_kv_heads, head_dim, max_seq, scale, &sp,
+                     S(stream));
 }
 
 int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream) {

@@ -187,6 +187,15 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Element strides of a KV cache: sequence b, position t, kv head h start at
+// cache + b*seq + t*pos + h*head. The reference's per-layer cache is [max_seq][n_kv*head_dim]
+// (pos = n_kv*head_dim, head = head_dim); the engine's is head-major, [n_kv][max_seq][head_dim]
+// per sequence (pos = head_dim, head = max_seq*head_dim), so each head's positions are
+// contiguous in memory.
+struct KvLayout {
+    long long seq, pos, head;
+};
+
 // Scratch of the split-KV attention (attention.cu): softmax statistics and per-chunk partial
 // outputs (the counters are unused).
 struct AttnSplit {

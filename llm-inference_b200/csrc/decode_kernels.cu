@@ -81,8 +81,8 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16 *out, const bf16 *in,
 
 // ------------------------------------------------------------------ qk_norm_rope
 // src/kernels.cu:301-403: one block of head_dim threads per q or k head (grid.x), one sequence
-// per grid.y. Strides are in elements between consecutive sequences; the caches of sequence b
-// start at key_cache + b * cache_stride (one layer's [max_seq, kv_dim] rows).
+// per grid.y. q/k/v strides are in elements between consecutive sequences; the cache row of
+// sequence b, position t, kv head h starts at key_cache + b*kv.seq + t*kv.pos + h*kv.head.
 struct RopeArgs {
     bf16 *q, *k;
     const bf16 *v;
@@ -90,8 +90,9 @@ struct RopeArgs {
     bf16 *key_cache, *value_cache;
     const int *pos;
     bf16 *q_tap, *k_tap;
-    long long q_stride, kv_stride, cache_stride;
-    int n_heads, head_dim, kv_dim;
+    long long q_stride, kv_stride;
+    KvLayout kv;
+    int n_heads, head_dim;
     int max_seq;  // > 0: positions are range-checked
     float eps, theta;
 };
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constan
     __syncthreads();
 
     const int half = a.head_dim / 2;
-    const size_t slot = (size_t)b * a.cache_stride + (size_t)pos * a.kv_dim + (size_t)head * a.head_dim;
+    const size_t slot = (size_t)b * a.kv.seq + (size_t)pos * a.kv.pos + (size_t)head * a.kv.head;
     if (i < half) {
         const int j = i;
         const float inv_freq = 1.0f / powf(a.theta, (float)(2 * j) / a.head_dim);
@@ -323,24 +324,37 @@ __device__ __forceinline__ uint32_t mix32(uint64_t x) {
     return (uint32_t)x;
 }
 
-__global__ void fill_normal_kernel(bf16 *dst, long long n, unsigned long long seed, float mean, float std) {
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const uint64_t c = seed * 0x9e3779b97f4a7c15ull + (uint64_t)i;
+// Block j (of n_blocks, block_len values each, starting block_stride elements apart) holds the
+// stream of seed + j: element i is Box-Muller over two hashed 24-bit uniforms of counter
+// (seed + j) * golden + i, so a block's values do not depend on the launch shape.
+__global__ void fill_normal_kernel(bf16 *dst, long long n_blocks, long long block_len, long long block_stride,
+                                   unsigned long long seed, float mean, float std) {
+    const long long n = n_blocks * block_len;
+    for (long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x; idx < n;
+         idx += (long long)gridDim.x * blockDim.x) {
+        const long long j = idx / block_len, i = idx - j * block_len;
+        const uint64_t c = (seed + (uint64_t)j) * 0x9e3779b97f4a7c15ull + (uint64_t)i;
         const float u1 = ((mix32(2 * c) >> 8) + 1) * (1.0f / 16777217.0f);  // (0, 1]
         const float u2 = (mix32(2 * c + 1) >> 8) * (1.0f / 16777216.0f);
         const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
-        dst[i] = __float2bfloat16(mean + std * z);
+        dst[j * block_stride + i] = __float2bfloat16(mean + std * z);
     }
 }
 
 }  // namespace
 
-int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s) {
-    if (!dst || n < 0) return Q3_ERR_ARG;
+int fill_normal_blocks(bf16 *dst, long long n_blocks, long long block_len, long long block_stride,
+                       unsigned long long seed, float mean, float std, cudaStream_t s) {
+    if (!dst || n_blocks < 0 || block_len < 0 || (n_blocks > 1 && block_stride < block_len)) return Q3_ERR_ARG;
+    const long long n = n_blocks * block_len;
     if (n == 0) return Q3_OK;
     const int blocks = (int)std::min<long long>((n + 255) / 256, 148LL * 16);
-    fill_normal_kernel<<<blocks, 256, 0, s>>>(dst, n, seed, mean, std);
+    fill_normal_kernel<<<blocks, 256, 0, s>>>(dst, n_blocks, block_len, block_stride, seed, mean, std);
     return record_cuda_error(cudaGetLastError());
+}
+
+int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s) {
+    return fill_normal_blocks(dst, 1, n, n, seed, mean, std, s);
 }
 
 unsigned take_error_decode() {
@@ -375,7 +389,7 @@ int rmsnorm(bf16 *out, const bf16 *in, const bf16 *weight, int rows, int dim, fl
 
 int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf16 *k_norm_w,
                  bf16 *key_cache, bf16 *value_cache, const int *pos, int n_rows, long long q_stride,
-                 long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
+                 long long kv_stride, KvLayout kv, int n_heads, int n_kv_heads, int head_dim,
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s) {
     if (!q || !k || !v || !q_norm_w || !k_norm_w || !key_cache || !value_cache || !pos) return Q3_ERR_ARG;
     if (head_dim % 32 != 0 || head_dim <= 0 || head_dim > 1024) return Q3_ERR_SHAPE;
@@ -394,10 +408,9 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
     a.k_tap = k_tap;
     a.q_stride = q_stride;
     a.kv_stride = kv_stride;
-    a.cache_stride = cache_stride;
+    a.kv = kv;
     a.n_heads = n_heads;
     a.head_dim = head_dim;
-    a.kv_dim = n_kv_heads * head_dim;
     a.max_seq = max_seq;
     a.eps = eps;
     a.theta = theta;

@@ -2,8 +2,10 @@
 // sequences on one GPU, with every buffer on the device and one CUDA graph per decode step.
 //
 // RunState (src/forward.cuh:6-25) becomes batched: activations [B, dim], one KV cache per layer
-// and sequence ([n_layers][B][max_seq][kv_dim], sequence b of layer l at
-// key_cache + (l*B + b)*max_seq*kv_dim), per-sequence token ids and positions in device memory.
+// and sequence, stored head-major -- [n_layers][B][n_kv_heads][max_seq][head_dim] -- so that the
+// positions of one (sequence, kv head) are contiguous and attention streams them in long runs
+// (the reference keeps one layer's heads interleaved per position, [max_seq][n_kv*head_dim]);
+// per-sequence token ids and positions live in device memory.
 // The launch order of one step is forward_kernels (src/forward.cu:118-193) followed by the
 // greedy argmax (:229-236), which here also feeds the next step on the device: it writes
 // next_token[b], advances pos[b] and appends the token to a history buffer, so a captured step
@@ -34,18 +36,20 @@ int embedding(bf16 *out, const bf16 *table, const int *tokens, int n_rows, int h
 int rmsnorm(bf16 *out, const bf16 *in, const bf16 *weight, int rows, int dim, float eps, cudaStream_t s);
 int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf16 *k_norm_w,
                  bf16 *key_cache, bf16 *value_cache, const int *pos, int n_rows, long long q_stride,
-                 long long kv_stride, long long cache_stride, int n_heads, int n_kv_heads, int head_dim,
+                 long long kv_stride, KvLayout kv, int n_heads, int n_kv_heads, int head_dim,
                  int max_seq, float eps, float theta, bf16 *q_tap, bf16 *k_tap, cudaStream_t s);
 int argmax_rows(const bf16 *x, int n, int n_rows, long long row_stride, int *out, int *next_token,
                 int *pos, int *history, int *step, int history_cap, cudaStream_t s);
 int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value_cache, float *scores, int ld,
-              const int *pos, int n_rows, long long q_stride, long long cache_stride, int n_heads, int n_kv_heads,
+              const int *pos, int n_rows, long long q_stride, KvLayout kv, int n_heads, int n_kv_heads,
               int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
 int score_ld(int max_seq);
 size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, AttnSplit *sp,
                                 float **scores, void *base);
 int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s);
+int fill_normal_blocks(bf16 *dst, long long n_blocks, long long block_len, long long block_stride,
+                       unsigned long long seed, float mean, float std, cudaStream_t s);
 }  // namespace q3
 
 using namespace q3;
@@ -90,7 +94,8 @@ int enqueue_step(q3_engine *e) {
     const q3_config &c = e->cfg;
     const int B = e->B, H = c.hidden_size, I = c.intermediate_size;
     const int qd = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
-    const long long seq_stride = (long long)e->max_seq * kvd;
+    const long long seq_stride = (long long)e->max_seq * kvd;  // one (layer, sequence): n_kv heads x max_seq rows
+    const KvLayout kv = {seq_stride, c.head_dim, (long long)e->max_seq * c.head_dim};
     const float scale = (float)(1.0 / sqrt((double)c.head_dim));
     cudaStream_t s = e->stream;
     const bool exact_attn = (e->flags & Q3_ENGINE_EXACT_ATTENTION) != 0;
@@ -104,10 +109,10 @@ int enqueue_step(q3_engine *e) {
         TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, B, qd, kvd,
                      H, s));
         TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, e->pos, B, qd,
-                         kvd, seq_stride, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps,
-                         c.rope_theta, nullptr, nullptr, s));
-        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), e->pos, B, qd, seq_stride,
-                      c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
+                         kvd, kv, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps, c.rope_theta,
+                         nullptr, nullptr, s));
+        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), e->pos, B, qd, kv, c.n_heads,
+                      c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
         TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, B, H, qd, nullptr, s));
         TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, B, H, c.rms_norm_eps, s));
         TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, B, I, H, nullptr, nullptr, s));
@@ -311,15 +316,14 @@ int q3_engine_sample_argmax(q3_engine *e, int *tokens_out) {
 int q3_engine_fill_kv_normal(q3_engine *e, int n_positions, unsigned long long seed) {
     if (!e || n_positions < 0 || n_positions > e->max_seq) return Q3_ERR_ARG;
     const q3_config &c = e->cfg;
-    const size_t kvd = (size_t)c.n_kv_heads * c.head_dim;
-    const size_t rows = (size_t)n_positions * kvd;
-    for (int l = 0; l < c.n_layers; l++)
-        for (int b = 0; b < e->B; b++) {
-            const size_t off = ((size_t)l * e->B + b) * e->max_seq * kvd;
-            const unsigned long long sk = seed * 1000003ull + (unsigned long long)(l * e->B + b) * 2;
-            TRY(fill_normal(e->key_cache + off, (long long)rows, sk, 0.0f, 1.0f, e->stream));
-            TRY(fill_normal(e->value_cache + off, (long long)rows, sk + 1, 0.0f, 1.0f, e->stream));
-        }
+    // One block per (layer, sequence, kv head): its first n_positions rows of the head-major cache.
+    const long long n_blocks = (long long)c.n_layers * e->B * c.n_kv_heads;
+    const long long head_rows = (long long)e->max_seq * c.head_dim;
+    const long long n = (long long)n_positions * c.head_dim;
+    const unsigned long long sk = seed * 1000003ull;
+    TRY(fill_normal_blocks(e->key_cache, n_blocks, n, head_rows, sk, 0.0f, 1.0f, e->stream));
+    TRY(fill_normal_blocks(e->value_cache, n_blocks, n, head_rows, sk + (unsigned long long)n_blocks, 0.0f, 1.0f,
+                           e->stream));
     return Q3_OK;
 }
 

@@ -31,6 +31,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// 128-byte swizzle operand with explicit offsets. K-major: rows of 128 bytes (64 K values), SBO
+// between 8-row groups, LBO unused. MN-major: each row of 128 bytes holds 64 consecutive M (or N)
+// values for one K index, 8 K rows form a 1024-byte swizzle atom; LBO is the byte distance to the
+// atom of the next 64 M values, SBO the distance to the next 8 K rows.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16) |
+           ((uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t accumulate) {
     asm volatile(

@@ -55,6 +55,8 @@ def check_close(mine, ref, absbound, what, extra=None):
     if extra is not None:
         bound = bound + np.asarray(extra, np.float32).reshape(-1)
     worst = np.abs(mf - rf) - bound
+    assert np.array_equal(np.isnan(mf), np.isnan(rf)), f"{what}: NaN where the reference has none (or the reverse)"
+    worst = np.nan_to_num(worst, nan=0.0)
     assert frac_over <= 0.005, f"{what}: {frac_over:.4%} of elements differ by more than 1 ulp (max {d.max()})"
     if worst.max() > 0:
         i = int(worst.argmax())
@@ -133,8 +135,25 @@ def test_batched_gate_up_qkv_lm_head(batch):
     assert q3.device_error() == 0
 
 
+def cache_strides(layout, max_seq, n_kv, hd):
+    """(seq, pos, head) element strides of a [B][max_seq][n_kv*hd] ("ref") or [B][n_kv][max_seq][hd]
+    ("head") cache."""
+    if layout == "ref":
+        return max_seq * n_kv * hd, n_kv * hd, hd
+    return n_kv * max_seq * hd, hd, max_seq * hd
+
+
+def to_layout(cache, layout, n_kv, hd):
+    """A [B][max_seq][n_kv*hd] cache re-laid out as `layout` (a copy)."""
+    if layout == "ref":
+        return cache.clone()
+    b, t, _ = cache.shape
+    return cache.view(b, t, n_kv, hd).permute(0, 2, 1, 3).contiguous()
+
+
+@pytest.mark.parametrize("layout", ["ref", "head"])
 @pytest.mark.parametrize("batch,n_heads,n_kv,hd", [(4, 32, 8, 128), (3, 16, 8, 128), (2, 4, 2, 64)])
-def test_batched_rope_and_split_attention(batch, n_heads, n_kv, hd):
+def test_batched_rope_and_split_attention(batch, n_heads, n_kv, hd, layout):
     g = torch.Generator(device="cuda").manual_seed(batch + n_heads)
     max_seq = 2600
     kvd = n_kv * hd
@@ -146,21 +165,31 @@ def test_batched_rope_and_split_attention(batch, n_heads, n_kv, hd):
     v = rn(g, batch, kvd)
     qn, kn = rn(g, hd, std=0.02, mean=1.0), rn(g, hd, std=0.02, mean=1.0)
     pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    strides = cache_strides(layout, max_seq, n_kv, hd)
     # batched rope writes row pos[b] of each sequence's cache; check against per-sequence drop-in
+    # calls on the reference layout, then compare in the tested layout
     kc2, vc2, q2, k2 = kc.clone(), vc.clone(), q.clone(), k.clone()
+    kl, vl = to_layout(kc, layout, n_kv, hd), to_layout(vc, layout, n_kv, hd)
     _lib.call("q3_qk_norm_rope_batched", q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr(), kn.data_ptr(),
-              kc.data_ptr(), vc.data_ptr(), max_seq * kvd, pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, 1e-6,
+              kl.data_ptr(), vl.data_ptr(), *strides, pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, 1e-6,
               1e6, None, None, stream())
     for b in range(batch):
         q3.qk_norm_rope_forward(q2[b], k2[b], v[b], qn, kn, kc2[b], vc2[b], pos[b:b + 1], n_heads, n_kv, hd, 1e-6, 1e6)
-    assert torch.equal(q, q2) and torch.equal(k, k2) and torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    assert torch.equal(q, q2) and torch.equal(k, k2)
+    assert torch.equal(kl, to_layout(kc2, layout, n_kv, hd)) and torch.equal(vl, to_layout(vc2, layout, n_kv, hd))
+    kc, vc = kc2, vc2
+    # rows past each sequence's position are never read by the reference: poison them
+    for b, p in enumerate(positions):
+        kc[b, p + 1:] = float("nan")
+        vc[b, p + 1:] = float("nan")
+    kl, vl = to_layout(kc, layout, n_kv, hd), to_layout(vc, layout, n_kv, hd)
 
     scale = float(np.float32(1.0 / math.sqrt(hd)))
     out = torch.empty(batch, n_heads * hd, dtype=torch.bfloat16, device="cuda")
     nbytes = _lib.load().q3_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq)
     scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
     for rep in range(2):  # the scratch counters must come back to zero: run twice
-        _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), max_seq * kvd,
+        _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), kl.data_ptr(), vl.data_ptr(), *strides,
                   scratch.data_ptr(), pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, scale, stream())
         ref = torch.empty_like(out)
         att = torch.empty(n_heads * max_seq, dtype=torch.float32, device="cuda")
