@@ -51,7 +51,7 @@ constexpr int K_STAGES = 2;
 constexpr int VT = 64;           // positions per staged V tile
 constexpr int V_STAGES = 3;
 constexpr int MAX_B = 1024;      // sequences per launch (prefix table in shared memory)
-constexpr int STATS_SMEM = 160 * 1024;
+constexpr int STATS_SMEM = 160 * 1024;  // stats kernel: upper bound of its score staging
 
 struct AttnArgs {
     const bf16 *q;        // sequence b: q + b*q_stride, heads concatenated
@@ -68,6 +68,7 @@ struct AttnArgs {
     int chunk_b;          // positions per pv item
     int sc_chunk;         // positions per scores item
     int max_chunks;       // split mode: capacity of `partial` along the chunk axis
+    int stats_cap;        // stats kernel: floats of shared memory for staged scores
     float scale;
 };
 
@@ -166,6 +167,7 @@ __device__ void softmax_stats(const AttnArgs &a, int b, int kvh, int len, float 
     const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
     const float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP) * a.ld;
     const int slice = max(THREADS, (cap / NREP) / THREADS * THREADS);  // a multiple of 128 positions
+    const bool resident = len <= slice;  // one slice holds every score: stage it once
     float mx[NREP], sm[NREP];
 #pragma unroll
     for (int h = 0; h < NREP; h++) {
@@ -175,12 +177,14 @@ __device__ void softmax_stats(const AttnArgs &a, int b, int kvh, int len, float 
     for (int pass = 0; pass < 2; pass++) {
         for (int t0 = 0; t0 < len; t0 += slice) {
             const int n = min(slice, len - t0);
-            __syncthreads();  // the previous slice has been read
+            if (pass == 0 || !resident) {
+                __syncthreads();  // the previous slice has been read
 #pragma unroll
-            for (int h = 0; h < NREP; h++) stage_scores(buf + h * slice, sc + (size_t)h * a.ld + t0, n);
-            cp_async_commit();
-            cp_async_wait<0>();
-            __syncthreads();
+                for (int h = 0; h < NREP; h++) stage_scores(buf + h * slice, sc + (size_t)h * a.ld + t0, n);
+                cp_async_commit();
+                cp_async_wait<0>();
+                __syncthreads();
+            }
             for (int t = tid; t < n; t += THREADS)
 #pragma unroll
                 for (int h = 0; h < NREP; h++) {
@@ -316,7 +320,7 @@ __global__ void __launch_bounds__(THREADS) attn_stats_kernel(const __grid_consta
     const int len = seq_len(a, b);
     if (len == 0) return;
     float m[NREP], s[NREP];
-    softmax_stats<NREP>(a, b, kvh, len, reinterpret_cast<float *>(smem), STATS_SMEM / 4, m, s);
+    softmax_stats<NREP>(a, b, kvh, len, reinterpret_cast<float *>(smem), a.stats_cap, m, s);
     if (threadIdx.x < NREP) {
         float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + threadIdx.x) * 2;
         st[0] = m[threadIdx.x];
@@ -595,7 +599,8 @@ constexpr int PV_ACC = 2;
 constexpr int PV_V_BYTES = PV_TILE * 128;      // one 64-dim half of a V tile
 constexpr int PV_P_OFF = 2 * PV_V_BYTES;       // P: 2 swizzle atoms of 16 rows x 128 B
 constexpr int PV_S_OFF = PV_P_OFF + 2 * 16 * 128;
-constexpr int PV_STAGE_BYTES = PV_S_OFF + 8 * PV_TILE * 4;  // scores of up to 8 heads
+constexpr int PV_T_OFF = PV_S_OFF + 8 * PV_TILE * 4;        // scores of up to 8 heads
+constexpr int PV_STAGE_BYTES = PV_T_OFF + 1024;             // the group's (max, sum) pairs
 
 struct PvTcPlan {
     int k_rows_per_seq, k_rows_per_head, k_cols_per_head;
@@ -666,6 +671,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
             const int row0 = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head;
+            // the group's statistics, from the 16-byte boundary below them (the stats region is
+            // padded to 256 bytes, so the rounded-up copy stays inside it)
+            const float *stp = a.stats + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * 2;
+            const uintptr_t st_al = reinterpret_cast<uintptr_t>(stp) & ~uintptr_t(15);
+            const uint32_t tbytes = (uint32_t)((reinterpret_cast<uintptr_t>(stp) - st_al + NREP * 8 + 15) & ~15u);
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
                 const int st = k % PV_STAGES;
                 if (k >= PV_STAGES && !mbar_wait(&empty[st], ((k / PV_STAGES) - 1) & 1, &g_dev_error)) {
@@ -675,7 +685,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int rows = min(PV_TILE, t1 - tt);
                 const uint32_t sbytes = (uint32_t)((rows + 3) / 4) * 16;  // within ld: ld is a multiple of 4
                 unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
-                mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + NREP * sbytes);
+                const bool first = tt == t0;
+                mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + NREP * sbytes + (first ? tbytes : 0));
+                if (first) bulk_g2s(base + PV_T_OFF, reinterpret_cast<const void *>(st_al), tbytes, &full[st]);
                 tma_load_2d(base, &tmV, it.kvh * pl.k_cols_per_head, row0 + tt, &full[st]);
                 tma_load_2d(base + PV_V_BYTES, &tmV, it.kvh * pl.k_cols_per_head + TMA_BK, row0 + tt, &full[st]);
 #pragma unroll
@@ -721,46 +733,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int quarter = warp % 4;
         const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
         const int d = quarter * 32 + lane;  // accumulator row = head dim
-        int k = 0, n_items = 0;
-        bool ok = true;
-        for (int item = i0; item < i1 && ok; item++, n_items++) {
-            const Item it = item_at(a, prefix, chunk, item, cur);
-            const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
-            float m[NREP], sum[NREP];
-#pragma unroll
-            for (int h = 0; h < NREP; h++) {
-                const float *stp = a.stats + ((size_t)it.b * a.n_heads + it.kvh * NREP + h) * 2;
-                m[h] = __ldcg(stp);
-                sum[h] = __ldcg(stp + 1);
-            }
-            for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
-                const int st = k % PV_STAGES;
-                if (!mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error)) {
-                    ok = false;
-                    break;
-                }
-                unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
-                const int rows = min(PV_TILE, t1 - tt);
-                const float *s_st = reinterpret_cast<const float *>(base + PV_S_OFF);
-                unsigned char *prow = base + PV_P_OFF + (t / 64) * 2048 + (t % 8) * 2;
-                const int c16 = (t % 64) / 8;
-#pragma unroll
-                for (int h = 0; h < NREP; h++) {
-                    const float p = t < rows ? round_bf16(expf(s_st[h * PV_TILE + t] - m[h]) / sum[h]) : 0.0f;
-                    *reinterpret_cast<bf16 *>(prow + h * 128 + ((c16 ^ (h & 7)) << 4)) = __float2bfloat16(p);
-                }
-                if (t >= rows) {  // V rows past the sequence: zero both halves of row t
-                    uint4 *v0 = reinterpret_cast<uint4 *>(base + t * 128);
-                    uint4 *v1 = reinterpret_cast<uint4 *>(base + PV_V_BYTES + t * 128);
-#pragma unroll
-                    for (int c = 0; c < 8; c++) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
-                }
-                fence_proxy_async();
-                mbar_arrive(&pfull[st]);
-            }
-            if (!ok) break;
-            const int buf = n_items % PV_ACC;
-            if (!mbar_wait(&acc_full[buf], (n_items / PV_ACC) & 1, &g_dev_error)) break;
+        // The epilogue of an item runs after the first tile of the next one has been handed to
+        // the MMA, so that waiting for the accumulator overlaps the next item's work.
+        Item pend = {};
+        int pend_n = -1;
+        auto epilogue = [&](const Item &it, int n_item) -> bool {
+            const int buf = n_item % PV_ACC;
+            if (!mbar_wait(&acc_full[buf], (n_item / PV_ACC) & 1, &g_dev_error)) return false;
             tc_fence_after();
             float acc[8];
             tmem_ld8(lane_addr + buf * 16, acc);
@@ -778,7 +757,57 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                     for (int h = 0; h < NREP; h++) part[((size_t)h * a.max_chunks + it.c) * a.head_dim + d] = acc[h];
                 }
             }
+            return true;
+        };
+        int k = 0, n_items = 0;
+        bool ok = true;
+        for (int item = i0; item < i1 && ok; item++, n_items++) {
+            const Item it = item_at(a, prefix, chunk, item, cur);
+            const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
+            float m[NREP], sum[NREP];
+            for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
+                const int st = k % PV_STAGES;
+                if (!mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error)) {
+                    ok = false;
+                    break;
+                }
+                unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
+                if (tt == t0) {  // the statistics came with the item's first tile
+                    const uintptr_t src = reinterpret_cast<uintptr_t>(a.stats + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * 2);
+                    const float *stp = reinterpret_cast<const float *>(base + PV_T_OFF + (src & 15));
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) {
+                        m[h] = stp[2 * h];
+                        sum[h] = stp[2 * h + 1];
+                    }
+                }
+                const int rows = min(PV_TILE, t1 - tt);
+                const float *s_st = reinterpret_cast<const float *>(base + PV_S_OFF);
+                unsigned char *prow = base + PV_P_OFF + (t / 64) * 2048 + (t % 8) * 2;
+                const int c16 = (t % 64) / 8;
+#pragma unroll
+                for (int h = 0; h < NREP; h++) {
+                    const float p = t < rows ? round_bf16(expf(s_st[h * PV_TILE + t] - m[h]) / sum[h]) : 0.0f;
+                    *reinterpret_cast<bf16 *>(prow + h * 128 + ((c16 ^ (h & 7)) << 4)) = __float2bfloat16(p);
+                }
+                if (t >= rows) {  // V rows past the sequence: zero both halves of row t
+                    uint4 *v0 = reinterpret_cast<uint4 *>(base + t * 128);
+                    uint4 *v1 = reinterpret_cast<uint4 *>(base + PV_V_BYTES + t * 128);
+#pragma unroll
+                    for (int c = 0; c < 8; c++) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+                }
+                fence_proxy_async();
+                mbar_arrive(&pfull[st]);
+                if (pend_n >= 0) {
+                    if (!epilogue(pend, pend_n)) ok = false;
+                    pend_n = -1;
+                    if (!ok) break;
+                }
+            }
+            pend = it;
+            pend_n = n_items;
         }
+        if (ok && pend_n >= 0) epilogue(pend, pend_n);
     }
     __syncwarp();
     tc_fence_before();
@@ -951,6 +980,18 @@ int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     return Q3_OK;
 }
 
+// Stats kernel with just enough shared memory for every score of its group (several CTAs per
+// SM, one wave), or STATS_SMEM slices for longer caches.
+template <int NREP>
+int launch_stats(AttnArgs a, cudaStream_t s) {
+    const long long need = (long long)NREP * ((a.max_seq + THREADS - 1) / THREADS * THREADS) * 4;
+    const size_t smem = (size_t)std::min<long long>(need, STATS_SMEM);
+    a.stats_cap = (int)(smem / 4);
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), smem));
+    Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), smem, s, 1, a));
+    return Q3_OK;
+}
+
 template <int NREP>
 int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
     PvTcPlan pl;
@@ -989,8 +1030,8 @@ int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     if (split && split_fast_path(a)) {
         int st = launch_scores_tc<NREP>(a, s);
         if (st != Q3_OK) return st;
-        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), STATS_SMEM));
-        Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), (size_t)STATS_SMEM, s, 1, a));
+        st = launch_stats<NREP>(a, s);
+        if (st != Q3_OK) return st;
         if (a.head_dim == 128 && a.chunk_b % PV_TILE == 0) {  // P.V on the tensor cores
             st = launch_pv_tc<NREP>(a, s);
             if (st != Q3_OK) return st;
@@ -1017,8 +1058,8 @@ int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     Q3_TRY_LAUNCH(launch(attn_scores_kernel<NREP>, dim3(grid_sc), dim3(SC_THREADS), sc_smem, s, 1, a));
     // stats
     if (split) {
-        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), STATS_SMEM));
-        Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), (size_t)STATS_SMEM, s, 1, a));
+        const int st = launch_stats<NREP>(a, s);
+        if (st != Q3_OK) return st;
     }
     // pv
     const size_t pv_smem = (size_t)V_STAGES * VT * a.head_dim * 2 + (size_t)V_STAGES * NREP * VT * 4 +

@@ -52,17 +52,41 @@ __global__ void embedding_kernel(bf16 *out, const bf16 *table, const int *tokens
 }
 
 // ------------------------------------------------------------------ rmsnorm
-// src/kernels.cu:25-71, one 256-thread block per row, same reduction order.
+// src/kernels.cu:25-71, one 256-thread block per row, same reduction order. Rows of up to
+// RMS_CACHE * 256 elements stay in registers between the two passes, and the weight, which no
+// kernel writes, is loaded before the wait on the previous kernel.
+constexpr int RMS_CACHE = 16;
+
 __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16 *out, const bf16 *in, const bf16 *weight,
                                                       int dim, float eps) {
     pdl_trigger();
+    const bool cached = dim <= RMS_CACHE * 256;
+    float wv[RMS_CACHE], xv[RMS_CACHE];
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < RMS_CACHE; j++) {
+            const int i = threadIdx.x + j * 256;
+            wv[j] = i < dim ? __bfloat162float(weight[i]) : 0.0f;
+        }
+    }
     pdl_wait();
     const bf16 *x = in + (size_t)blockIdx.x * dim;
     bf16 *y = out + (size_t)blockIdx.x * dim;
     float sum = 0.0f;
-    for (int i = threadIdx.x; i < dim; i += 256) {
-        const float v = __bfloat162float(x[i]);
-        sum = __fmaf_rn(v, v, sum);
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < RMS_CACHE; j++) {
+            const int i = threadIdx.x + j * 256;
+            xv[j] = i < dim ? __bfloat162float(x[i]) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < RMS_CACHE; j++)
+            if (threadIdx.x + j * 256 < dim) sum = __fmaf_rn(xv[j], xv[j], sum);
+    } else {
+        for (int i = threadIdx.x; i < dim; i += 256) {
+            const float v = __bfloat162float(x[i]);
+            sum = __fmaf_rn(v, v, sum);
+        }
     }
     for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
     __shared__ float warp_sums[8];
@@ -72,10 +96,18 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16 *out, const bf16 *in,
 #pragma unroll
     for (int w = 0; w < 8; w++) total += warp_sums[w];
     const float inv_rms = rsqrtf(total / dim + eps);
-    for (int i = threadIdx.x; i < dim; i += 256) {
-        const float v = __bfloat162float(x[i]);
-        const bf16 normed = __float2bfloat16(v * inv_rms);
-        y[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(weight[i]));
+    if (cached) {
+#pragma unroll
+        for (int j = 0; j < RMS_CACHE; j++) {
+            const int i = threadIdx.x + j * 256;
+            if (i < dim) y[i] = __float2bfloat16(round_bf16(xv[j] * inv_rms) * wv[j]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < dim; i += 256) {
+            const float v = __bfloat162float(x[i]);
+            const bf16 normed = __float2bfloat16(v * inv_rms);
+            y[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(weight[i]));
+        }
     }
 }
 
