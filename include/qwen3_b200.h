@@ -45,6 +45,7 @@ enum q3_status {
     Q3_ERR_CUDA = 3,     /* a CUDA call failed; q3_last_cuda_error() gives the cudaError_t */
     Q3_ERR_DEVICE = 4,   /* the current device is not sm_100 (B200) */
     Q3_ERR_ARG = 5,      /* a null pointer or an invalid option */
+    Q3_ERR_SCRATCH_LIMIT = 6, /* the shape needs more scratch than Q3_ATTENTION_STATIC_SCRATCH_BYTES */
 };
 
 /* Text for a q3_status value. */
@@ -164,6 +165,30 @@ int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
                          long long cache_seq_stride, long long cache_pos_stride, long long cache_head_stride,
                          void *scratch, const int *d_pos, int batch, int n_heads, int n_kv_heads, int head_dim,
                          int max_seq, float scale, void *stream);
+
+/* Size of the device array that q3_attention_batched_static uses as its scratch (32 MiB; every
+ * GPU that loads this library holds it until the process exits). Enough, for example, for 32
+ * sequences x 32 query heads x 4352 positions at head_dim 128. */
+#define Q3_ATTENTION_STATIC_SCRATCH_BYTES (32u << 20)
+
+/* q3_attention_batched without a scratch argument, for callers that cannot allocate device
+ * memory while they run: a host runtime that reserves all of its GPU memory in one pool at
+ * start-up, a plugin living inside another framework's memory manager, or a serving loop where
+ * an allocation could block or fail mid-request. It allocates nothing: the scratch is a fixed
+ * array in the library (Q3_ATTENTION_STATIC_SCRATCH_BYTES per device), and it runs the same
+ * kernels as q3_attention_batched, so the results are the same. This entry point has no
+ * counterpart in the reference.
+ *   - Shapes whose scratch (q3_attention_scratch_bytes) exceeds the array return
+ *     Q3_ERR_SCRATCH_LIMIT and launch nothing.
+ *   - The first call on a device looks up the array's device address (once per device, with
+ *     that device current); make that first call before any stream capture.
+ *   - Every call on a device shares the one array. Calls that overlap on the GPU (other
+ *     streams, other host threads) race on it; serialize them. Nothing in the array needs
+ *     clearing between calls: each call writes every scratch value before using it. */
+int q3_attention_batched_static(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cache,
+                                const q3_bf16 *value_cache, long long cache_seq_stride, long long cache_pos_stride,
+                                long long cache_head_stride, const int *d_pos, int batch, int n_heads,
+                                int n_kv_heads, int head_dim, int max_seq, float scale, void *stream);
 
 /* out[b] = argmax of x[b][0..n) with argmax_forward's tie and NaN rules. */
 int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream);

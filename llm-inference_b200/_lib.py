@@ -47,6 +47,7 @@ SIGNATURES: dict[str, list] = {
     "q3_qk_norm_rope_batched": [_P, _P, _P, _P, _P, _P, _P, _LL, _LL, _LL, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P],
     "q3_attention_scratch_bytes": [_I, _I, _I, _I, _I],
     "q3_attention_batched": [_P, _P, _P, _P, _LL, _LL, _LL, _P, _P, _I, _I, _I, _I, _I, _F, _P],
+    "q3_attention_batched_static": [_P, _P, _P, _P, _LL, _LL, _LL, _P, _I, _I, _I, _I, _I, _F, _P],
     "q3_argmax_batched": [_P, _P, _I, _I, _P],
     "q3_fill_normal_bf16": [_P, _LL, ctypes.c_ulonglong, _F, _F, _P],
     "q3_weight_bytes_per_step": [_P],

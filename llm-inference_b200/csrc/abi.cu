@@ -124,6 +124,7 @@ const char *q3_status_string(int status) {
         case Q3_ERR_CUDA: return "a CUDA call failed";
         case Q3_ERR_DEVICE: return "the current device is not sm_100 (B200)";
         case Q3_ERR_ARG: return "a null pointer or an invalid option";
+        case Q3_ERR_SCRATCH_LIMIT: return "the shape needs more scratch than the static scratch array holds";
         default: return "unknown status";
     }
 }
