@@ -89,15 +89,23 @@ __device__ __forceinline__ int seq_len(const AttnArgs &a, int b) {
     return p + 1;
 }
 
-// Item table in shared memory: items of sequence b occupy [prefix[b], prefix[b+1]).
+// Item table in shared memory (PREFIX_INTS(B) ints): items of sequence b occupy
+// [prefix[b], prefix[b+1]), and prefix[B + 1 + b] holds its length, so that walking the items
+// reads no global memory. The positions are loaded by all threads at once.
+#define PREFIX_INTS(B) (2 * (B) + 1)
 __device__ int build_prefix(const AttnArgs &a, int chunk, int *prefix) {
+    int *lens = prefix + a.B + 1;
+    for (int b = threadIdx.x; b < a.B; b += blockDim.x) {
+        const int n = seq_len(a, b);
+        lens[b] = n;
+        if (n == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
+    }
+    __syncthreads();
     if (threadIdx.x == 0) {
         int total = 0;
         for (int b = 0; b < a.B; b++) {
             prefix[b] = total;
-            const int n = seq_len(a, b);
-            if (n == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
-            total += a.n_kv * ((n + chunk - 1) / chunk);
+            total += a.n_kv * ((lens[b] + chunk - 1) / chunk);
         }
         prefix[a.B] = total;
     }
@@ -114,7 +122,7 @@ __device__ __forceinline__ Item find_item(const AttnArgs &a, const int *prefix, 
     int b = 0;
     while (prefix[b + 1] <= item) b++;
     it.b = b;
-    it.len = seq_len(a, b);
+    it.len = prefix[a.B + 1 + b];
     it.nc = (it.len + chunk - 1) / chunk;
     const int r = item - prefix[b];
     it.kvh = r / it.nc;
@@ -139,7 +147,7 @@ __device__ __forceinline__ Item item_at(const AttnArgs &a, const int *prefix, in
     while (prefix[b + 1] <= item) b++;
     Item it;
     it.b = b;
-    it.len = seq_len(a, b);
+    it.len = prefix[a.B + 1 + b];
     it.nc = (it.len + chunk - 1) / chunk;
     const int r = item - prefix[b];
     it.kvh = r / it.nc;
@@ -556,7 +564,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
         for (int k = 0; k < n; k++) {
             const int buf = k % TC_ACC;
-            if (!mbar_wait(&acc_full[buf], (k / TC_ACC) & 1, &g_dev_error)) break;
+            // warp-uniform exit: tcgen05.ld below is warp-collective
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (k / TC_ACC) & 1, &g_dev_error))) break;
             tc_fence_after();
             float acc[8];
             tmem_ld8(lane_addr + buf * TC_N, acc);
@@ -739,7 +748,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int pend_n = -1;
         auto epilogue = [&](const Item &it, int n_item) -> bool {
             const int buf = n_item % PV_ACC;
-            if (!mbar_wait(&acc_full[buf], (n_item / PV_ACC) & 1, &g_dev_error)) return false;
+            // warp-uniform exit: tcgen05.ld below is warp-collective
+            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (n_item / PV_ACC) & 1, &g_dev_error))) return false;
             tc_fence_after();
             float acc[8];
             tmem_ld8(lane_addr + buf * 16, acc);
@@ -767,8 +777,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             float m[NREP], sum[NREP];
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
                 const int st = k % PV_STAGES;
-                if (!mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error)) {
-                    ok = false;
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error))) {
+                    ok = false;  // the whole warp leaves: the epilogue's tcgen05.ld is warp-collective
                     break;
                 }
                 unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
@@ -972,7 +982,7 @@ int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     CUtensorMap mk, mq;
     if (!make_map_strided(&mk, a.kc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, TC_TILE)) return Q3_ERR_ARG;
     if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TC_N)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)(a.B + 1) * 4;
+    const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)PREFIX_INTS(a.B) * 4;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_tc_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + TC_TILE - 1) / TC_TILE);
     const int grid = (int)std::min<long long>(max_items, num_sms());
@@ -1003,7 +1013,7 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
                ((uint32_t)(128 >> 4) << 24);
     CUtensorMap mv;
     if (!make_map_strided(&mv, a.vc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)(a.B + 1) * 4;
+    const size_t smem = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)PREFIX_INTS(a.B) * 4;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
     const int grid = (int)std::min<long long>(max_items, num_sms());
@@ -1026,7 +1036,7 @@ template <int NREP>
 int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     const int nsm = num_sms();
     const bool split = a.stats != nullptr;
-    const size_t prefix_bytes = (size_t)(a.B + 1) * 4;
+    const size_t prefix_bytes = (size_t)PREFIX_INTS(a.B) * 4;
     if (split && split_fast_path(a)) {
         int st = launch_scores_tc<NREP>(a, s);
         if (st != Q3_OK) return st;

@@ -22,10 +22,13 @@
 // Work: weight rows are cut into tiles of R <= 128 rows and K into S slices; a tile's S slices
 // run on the S CTAs of one thread-block cluster. R and S are chosen so that tiles x S fill the
 // SMs in one wave with as many weight bytes per pipeline stage as possible (o_proj and down,
-// 2560 rows: S = 4). With S > 1 each CTA stages its fp32 partial tile in shared memory and,
-// after a cluster barrier, reduces its share of the tile's rows over the S CTAs' partials
-// (distributed shared memory, in rank order) before the epilogue. With S = 1 a persistent
-// grid walks the tiles. The gate and up projections share a tile (two accumulators side by
+// 2560 rows: S = 4). With S > 1, ranks 1..S-1 of the cluster write their fp32 partial tiles
+// into a receive buffer in rank 0's shared memory (distributed shared memory stores, then a
+// release arrive on rank 0's mbarrier) and exit; rank 0 adds them to its own accumulator in rank
+// order and runs the epilogue. No cluster barrier sits at the end of the kernel: the only one is
+// split into an arrive after set-up and a wait before the epilogue, which guarantees that rank
+// 0's mbarrier is initialized before anyone arrives on it. With S = 1 a persistent grid
+// walks the tiles. The gate and up projections share a tile (two accumulators side by
 // side in TMEM).
 //
 // Arithmetic note: the fp32 sums run in the tensor core's order, not the reference's
@@ -57,8 +60,16 @@ constexpr int BK = 64;            // K per stage: 64 bf16 = one 128-byte swizzle
 constexpr int TILE_M = 128;       // MMA M
 constexpr int MAX_STAGES = 12;
 constexpr int KSUB = 4;           // 64-column sub-tiles per stage: 512 contiguous bytes per weight row
-constexpr size_t SMEM_BUDGET = 112 * 1024;  // leaves room for a co-resident successor kernel
+#ifndef Q3_GEMM_SMEM_BUDGET_KB
+#define Q3_GEMM_SMEM_BUDGET_KB 112  // leaves room for a co-resident successor kernel
+#endif
+constexpr size_t SMEM_BUDGET = (size_t)Q3_GEMM_SMEM_BUDGET_KB * 1024;
+#ifndef Q3_GEMM_MAX_SPLIT
+#define Q3_GEMM_MAX_SPLIT 8  // largest K split (cluster size) the planner considers
+#endif
 constexpr size_t SMEM_MAX = 220 * 1024;
+constexpr int BAR_BYTES = 256;  // mbarriers and the TMEM slot after the stage ring
+constexpr int RES_TMA_MAX_BP = 64;  // residual tiles loaded by TMA up to this padded batch
 
 enum Epi : int { PLAIN = 0, RESIDUAL = 1, QKV = 2, GATE_UP = 3 };
 
@@ -78,9 +89,50 @@ struct TcArgs {
     int a_tile_bytes;              // shared bytes of one weight tile: R rows rounded up to 8, x 128
     uint32_t idesc;
     uint32_t tmem_cols;
+    int res_tma;                   // RESIDUAL: rank 0 loads its tile's residual x [Bp, R] by TMA
+    int res_off;                   // shared-memory offset of that tile (from the aligned base)
 };
 
 // ---------------------------------------------------------------- kernel
+
+// Cluster barrier in two halves (every thread of every CTA of the cluster executes each once).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+    asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait;" ::: "memory"); }
+
+// Arrive on the mbarrier at the same shared-memory offset in cluster CTA `rank`, with release
+// semantics at cluster scope (this thread's earlier stores, remote ones included, are visible
+// to a thread that observes the phase with an acquire wait).
+__device__ __forceinline__ void mbar_arrive_remote(uint64_t *bar, unsigned rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(bar)), "r"(rank));
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(remote) : "memory");
+}
+
+// mbar_wait with acquire semantics at cluster scope (for arrivals from other CTAs).
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *err) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const uint64_t start = globaltimer();
+    while (!mbar_try_wait_cluster(bar, parity)) {
+        if (globaltimer() - start > WAIT_LIMIT_NS) {
+            atomicOr(err, DEV_ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
 
 __device__ __forceinline__ void tile_coords(const TcArgs &a, int t, int &mat, int &row0) {
     mat = 0;
@@ -92,7 +144,7 @@ template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                    const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmX,
-                   const __grid_constant__ TcArgs a) {
+                   const __grid_constant__ CUtensorMap tmR, const __grid_constant__ TcArgs a) {
     constexpr int NA = EPI == GATE_UP ? 2 : 1;  // weight tiles per stage (gate and up)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned base for the swizzled tiles
@@ -101,7 +153,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     uint64_t *empty = full + a.stages;
     uint64_t *acc_full = empty + a.stages;
     uint64_t *acc_empty = acc_full + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 1);
+    uint64_t *recv_full = acc_empty + 1;  // split-K, rank 0: the other ranks' partial tiles arrived
+    uint64_t *res_full = recv_full + 1;   // the residual tile arrived
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_full + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int S = a.stages;
@@ -113,11 +167,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, EPI_THREADS);
+        if (a.splits > 1) mbar_init(recv_full, (a.splits - 1) * EPI_THREADS);
+        mbar_init(res_full, 1);
         fence_barrier_init();
         prefetch_tmap(&tmA0);
         prefetch_tmap(&tmX);
         if (EPI == GATE_UP || EPI == QKV) prefetch_tmap(&tmA1);
         if (EPI == QKV) prefetch_tmap(&tmA2);
+        if (EPI == RESIDUAL && a.res_tma) prefetch_tmap(&tmR);
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -129,6 +186,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // split-K: rank 0's recv_full must be initialized before any rank arrives on it. Every
+    // thread arrives here and waits just before the epilogue, long after.
+    if (a.splits > 1) cluster_arrive_relaxed();
     pdl_trigger();
 
     // split-K: the S CTAs of a cluster share tile blockIdx.x / S, rank r takes K steps [k0, k1)
@@ -181,6 +241,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int pre = min(S, total_steps);
         for (int it = 0; it < pre; it++) issue_weights(it);  // weights do not depend on the previous kernel
         pdl_wait();
+        const bool res_load = EPI == RESIDUAL && a.res_tma && rank == 0 && my_tiles > 0;
+        if (res_load) {  // x rows of this tile for every batch row: read by the epilogue
+            int mat, row0;
+            tile_coords(a, tile_base, mat, row0);
+            mbar_arrive_expect_tx(res_full, (uint32_t)(a.R * a.Bp * 2));
+            tma_load_2d(smem + a.res_off, &tmR, row0, 0, res_full);
+        }
         for (int it = 0; it < pre; it++) issue_x(it);
         int it = pre;
         for (; it < total_steps; it++) {
@@ -193,6 +260,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         // leave no copy in flight into this CTA's shared memory
         for (int j = max(0, it - S); j < it; j++) mbar_wait(&full[j % S], (j / S) & 1, &g_dev_error);
+        if (res_load) mbar_wait(res_full, 0, &g_dev_error);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer
         int it = 0;
@@ -231,95 +299,51 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 
     __syncwarp();
-    if (S_split > 1) {
-        // ---------------- split-K epilogue: partial tile -> shared memory -> cluster reduction
-        // (one tile per cluster; the pipeline ring is idle and is reused for the partial tile)
-        const int ld = NA * a.Bp + 1;  // padded row: conflict-free column writes
-        float *part = reinterpret_cast<float *>(smem);
+    if (S_split > 1) cluster_wait();
+    if (S_split > 1 && rank > 0) {
+        // ---------------- split-K, ranks 1..S-1: push the fp32 partial tile into rank 0's
+        // receive buffer (distributed shared memory) and leave; nothing reads this CTA's memory.
         if (warp >= 2 && my_tiles > 0) {
             const int quarter = warp % 4;
             const int row_local = quarter * 32 + lane;
             const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-            if (!mbar_wait(acc_full, 0, &g_dev_error)) ok = false;
+            const int ldr = NA * a.Bp + 4;
+            float *recv = reinterpret_cast<float *>(smem + (size_t)a.stages * a.stage_bytes + BAR_BYTES);
+            float *dst = cg::this_cluster().map_shared_rank(recv, 0) + ((size_t)(rank - 1) * a.R + row_local) * ldr;
+            const bool got = mbar_wait(acc_full, 0, &g_dev_error);
             tc_fence_after();
+            // tcgen05.ld is warp-collective (.sync.aligned): every lane issues it; only the
+            // stores are guarded
+            const bool store = got && row_local < a.R;
             for (int c0 = 0; c0 < NA * a.Bp; c0 += 8) {
-                float acc[8];
-                tmem_ld8(lane_addr + c0, acc);
+                float v[8];
+                tmem_ld8(lane_addr + c0, v);
                 tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 8; j++) part[row_local * ld + c0 + j] = acc[j];
+                if (store) {
+                    reinterpret_cast<float4 *>(dst + c0)[0] = make_float4(v[0], v[1], v[2], v[3]);
+                    reinterpret_cast<float4 *>(dst + c0)[1] = make_float4(v[4], v[5], v[6], v[7]);
+                }
             }
             tc_fence_before();
+            mbar_arrive_remote(recv_full, 0);  // release: the stores above are visible to rank 0
         }
-        cg::cluster_group cluster = cg::this_cluster();
-        cluster.sync();
-        if (my_tiles > 0) {
-            pdl_wait();
-            int mat, row0;
-            tile_coords(a, tile_base, mat, row0);
-            bf16 *o = EPI == QKV ? (mat == 0 ? a.out0 : mat == 1 ? a.out1 : a.out2) : a.out0;
-            const long long ostride = a.rows[mat];
-            const int r_lo = a.R * rank / S_split, r_hi = a.R * (rank + 1) / S_split;
-            const int nr = r_hi - r_lo;
-            const float *peer[8];
-            for (int q = 0; q < S_split; q++) peer[q] = cluster.map_shared_rank(part, q);
-            // Items (row, b), consecutive threads on consecutive rows; EB items per thread at a
-            // time with every load (partials of all ranks, the residual) issued before any use.
-            constexpr int EB = 4;
-            const int n_items = nr * a.B;
-            for (int base = 0; base < n_items; base += EB * TC_THREADS) {
-                float acc[EB], acc2[EB], xr[EB];
-                int idx_m[EB], idx_b[EB];
-#pragma unroll
-                for (int e = 0; e < EB; e++) {
-                    const int i = base + e * TC_THREADS + (int)threadIdx.x;
-                    idx_b[e] = i < n_items ? i / nr : -1;
-                    idx_m[e] = i < n_items ? r_lo + i % nr : 0;
-                    if (idx_b[e] >= 0 && row0 + idx_m[e] >= a.rows[mat]) idx_b[e] = -1;
-                    acc[e] = acc2[e] = 0.0f;
-                    xr[e] = 0.0f;
-                    if (EPI == RESIDUAL && idx_b[e] >= 0)
-                        xr[e] = __bfloat162float(o[(size_t)idx_b[e] * ostride + row0 + idx_m[e]]);
-                }
-                for (int q = 0; q < S_split; q++) {
-#pragma unroll
-                    for (int e = 0; e < EB; e++) {
-                        if (idx_b[e] < 0) continue;
-                        acc[e] += peer[q][idx_m[e] * ld + idx_b[e]];
-                        if (EPI == GATE_UP) acc2[e] += peer[q][idx_m[e] * ld + a.Bp + idx_b[e]];
-                    }
-                }
-#pragma unroll
-                for (int e = 0; e < EB; e++) {
-                    if (idx_b[e] < 0) continue;
-                    const size_t idx = (size_t)idx_b[e] * ostride + row0 + idx_m[e];
-                    if (EPI == PLAIN || EPI == QKV) {
-                        o[idx] = __float2bfloat16(acc[e]);
-                    } else if (EPI == RESIDUAL) {
-                        const bf16 y = __float2bfloat16(acc[e]);
-                        if (a.tap0) a.tap0[idx] = y;
-                        o[idx] = __float2bfloat16(xr[e] + __bfloat162float(y));
-                    } else {
-                        const bf16 gate = __float2bfloat16(acc[e]), up = __float2bfloat16(acc2[e]);
-                        if (a.tap0) {
-                            a.tap0[idx] = gate;
-                            a.tap1[idx] = up;
-                        }
-                        const float gv = __bfloat162float(gate), uv = __bfloat162float(up);
-                        o[idx] = __float2bfloat16(round_bf16(gv / (1.0f + expf(-gv))) * uv);
-                    }
-                }
-            }
-        }
-        cluster.sync();  // every CTA's partial tile stays alive until all ranks have read it
     } else if (warp >= 2) {
-    // ---------------- epilogue (warps 2-5, one accumulator row per thread)
+    // ---------------- epilogue (warps 2-5, one accumulator row per thread). With split-K this
+    // is rank 0 of the cluster: its own partial (K steps of rank 0) plus the received partials
+    // of ranks 1..S-1, added in rank order.
     pdl_wait();
     const int quarter = warp % 4;
     const int row_local = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
+    const int ldr = NA * a.Bp + 4;
+    const float *recv = reinterpret_cast<const float *>(smem + (size_t)a.stages * a.stage_bytes + BAR_BYTES) +
+                        (size_t)row_local * ldr;
     for (int tl = 0; tl < my_tiles; tl++) {
-        if (!mbar_wait(acc_full, tl & 1, &g_dev_error)) {
+        bool got = mbar_wait(acc_full, tl & 1, &g_dev_error);
+        if (got && S_split > 1) got = mbar_wait_cluster(recv_full, 0, &g_dev_error);
+        if (got && EPI == RESIDUAL && a.res_tma) got = mbar_wait(res_full, 0, &g_dev_error);
+        // the warp leaves together, never splitting around the warp-collective tcgen05.ld below
+        if (!__all_sync(0xffffffffu, got)) {
             ok = false;
             break;
         }
@@ -337,6 +361,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (EPI == GATE_UP) tmem_ld8(lane_addr + a.Bp + c0, acc2);
             tmem_wait_ld();
             if (!valid) continue;
+            for (int q = 1; q < S_split; q++) {
+                const float *pq = recv + (size_t)(q - 1) * a.R * ldr;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    acc[j] += pq[c0 + j];
+                    if (EPI == GATE_UP) acc2[j] += pq[a.Bp + c0 + j];
+                }
+            }
+            float xr[8];
+            if (EPI == RESIDUAL) {  // the residual tile in shared memory, else 8 loads issued together
+                const bf16 *rt = reinterpret_cast<const bf16 *>(smem + a.res_off) + row_local;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    const int b = c0 + j;
+                    xr[j] = a.res_tma ? __bfloat162float(rt[(size_t)b * a.R])
+                                      : (b < a.B ? __bfloat162float(o[(size_t)b * ostride + m]) : 0.0f);
+                }
+            }
 #pragma unroll
             for (int j = 0; j < 8; j++) {
                 const int b = c0 + j;
@@ -347,7 +389,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 } else if (EPI == RESIDUAL) {
                     const bf16 y = __float2bfloat16(acc[j]);
                     if (a.tap0) a.tap0[idx] = y;
-                    o[idx] = __float2bfloat16(__bfloat162float(o[idx]) + __bfloat162float(y));
+                    o[idx] = __float2bfloat16(xr[j] + __bfloat162float(y));
                 } else {
                     const bf16 gate = __float2bfloat16(acc[j]);
                     const bf16 up = __float2bfloat16(acc2[j]);
@@ -402,20 +444,30 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
         for (int i = 0; i < n_mat; i++) n += (a.rows[i] + R - 1) / R;
         return n;
     };
+    // Residual x tile by TMA: its first column must sit on a 16-byte boundary, so R is a
+    // multiple of 8 (as are the rows, for the row pitch); small batches only.
+    const bool res_cand = EPI == RESIDUAL && a.Bp <= RES_TMA_MAX_BP && a.rows[0] % 8 == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.out0) & 15) == 0;
+    const int r_step = res_cand ? 8 : 1;
+    auto res_bytes = [&](int R_) { return res_cand ? (size_t)R_ * a.Bp * 2 : (size_t)0; };
     // Plan (R rows per tile, S K-slices): every cluster of S CTAs resident in one wave (checked
     // with the occupancy API, since clusters must fit inside one GPC), minimizing the work of the
     // busiest SM: K stages of its CTAs times their rows (rows below 64 count as 64).
     auto smem_for = [&](int R_, int S_, int *stages_out) {
         const int at = (R_ + 7) / 8 * 8 * BK * 2;
         const int sb = a.ksub * (NA * at + a.Bp * BK * 2);
-        int st = (int)std::min<size_t>(MAX_STAGES, (SMEM_BUDGET - 1024 - 256) / sb);
+        // split-K: rank 0 receives the other ranks' fp32 partial tiles after the barriers
+        const size_t recv = S_ > 1 ? (size_t)(S_ - 1) * R_ * (NA * a.Bp + 4) * 4 : 0;
+        const size_t room = SMEM_BUDGET - 1024 - BAR_BYTES - res_bytes(R_);
+        int st = room > recv ? (int)std::min<size_t>(MAX_STAGES, (room - recv) / sb) : 0;
         st = std::max(st, 2);
-        if (S_ > 1 && (size_t)st * sb < (size_t)TILE_M * (NA * a.Bp + 1) * 4)
-            st = (int)(((size_t)TILE_M * (NA * a.Bp + 1) * 4 + sb - 1) / sb);
         // the M = 128 MMA reads up to (128 - R) rows past a weight tile: slack beyond the last stage
         const int over = (TILE_M - (R_ + 7) / 8 * 8) * BK * 2 - a.ksub * a.Bp * BK * 2;
         if (stages_out) *stages_out = st;
-        return (size_t)1024 + (size_t)st * sb + 256 + (size_t)std::max(over, 0);
+        // the over-read may land in the receive buffer: it only feeds accumulator rows never read;
+        // the residual tile follows, 128-byte aligned
+        const size_t tail = ((size_t)st * sb + BAR_BYTES + std::max<size_t>((size_t)std::max(over, 0), recv) + 127) / 128 * 128;
+        return (size_t)1024 + tail + res_bytes(R_);
     };
     auto resident = [&](int S_, size_t smem_) {
         int n = 0;
@@ -462,11 +514,12 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
                 cached = true;
             }
     }
-    for (int S = 1; !cached && S <= 8 && S <= a.nk; S *= 2) {
+    for (int S = 1; !cached && S <= Q3_GEMM_MAX_SPLIT && S <= a.nk; S *= 2) {
         int slots = nsm / S, r = 0;
         for (int pass = 0; pass < 2; pass++) {
             r = std::max(8, (int)((total_rows + slots - 1) / std::max(slots, 1)));
-            while (r <= TILE_M && tiles_for(r) > slots) r++;
+            r = (r + r_step - 1) / r_step * r_step;
+            while (r <= TILE_M && tiles_for(r) > slots) r += r_step;
             if (r > TILE_M) break;
             slots = std::min(slots, resident(S, smem_for(r, S, nullptr)));
             if (slots <= 0) {
@@ -511,13 +564,19 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
     const size_t smem = smem_for(R, a.splits, &stages);
     a.stages = stages;
     if (smem > SMEM_MAX) return Q3_ERR_SHAPE;
+    // one tile per CTA (or cluster): the residual tile is loaded once, at the start
+    const int grid_ctas = a.splits > 1 ? a.n_tiles * a.splits : std::min(nsm, a.n_tiles);
+    a.res_tma = res_cand && R % 8 == 0 && a.n_tiles * a.splits <= grid_ctas ? 1 : 0;
+    a.res_off = (int)(smem - 1024 - res_bytes(R));
     uint32_t cols = 32;
     while (cols < (uint32_t)(NA * a.Bp)) cols *= 2;
     a.tmem_cols = cols;
     // kind::f16 instruction descriptor: fp32 accumulate, bf16 A and B, both K-major, N = Bp, M = 128
     a.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.Bp >> 3) << 17) | ((uint32_t)(TILE_M >> 4) << 24);
 
-    CUtensorMap m0, m1, m2, mx;
+    CUtensorMap m0, m1, m2, mx, mr;
+    memset(&mr, 0, sizeof(mr));
+    if (a.res_tma && !make_map_plain(&mr, a.out0, a.B, a.rows[0], a.rows[0], a.Bp, R)) return Q3_ERR_ARG;
     memset(&m1, 0, sizeof(m1));
     memset(&m2, 0, sizeof(m2));
     if (!make_map(&m0, w0, a.rows[0], a.K, R)) return Q3_ERR_ARG;
@@ -529,7 +588,7 @@ int launch_tc(TcArgs a, const bf16 *w0, const bf16 *w1, const bf16 *w2, const bf
 
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(tc_gemm_kernel<EPI>), smem));
     const int grid = a.splits > 1 ? a.n_tiles * a.splits : std::min(nsm, a.n_tiles);
-    Q3_TRY_LAUNCH(launch(tc_gemm_kernel<EPI>, dim3(grid), dim3(TC_THREADS), smem, stream, a.splits, m0, m1, m2, mx, a));
+    Q3_TRY_LAUNCH(launch(tc_gemm_kernel<EPI>, dim3(grid), dim3(TC_THREADS), smem, stream, a.splits, m0, m1, m2, mx, mr, a));
     return Q3_OK;
 }
 

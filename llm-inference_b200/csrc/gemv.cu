@@ -7,12 +7,13 @@
 // points. Splitting a row into column segments keeps that order because every segment but
 // the last is a multiple of 32 chunks.
 //
-// Memory pipeline (what is new): a persistent grid of one CTA per SM owns a balanced,
-// contiguous range of output rows. A producer warp streams the CTA's weight rows through a
-// ring of shared-memory stages with cp.async.bulk (completion on mbarriers), evict-first in
-// L2, and starts doing so before the programmatic-dependency wait, because weights never
-// depend on the previous kernel; eight consumer warps read the stages. The stage ring keeps
-// ~64 KB of weights in flight per SM.
+// Memory pipeline (what is new): persistent warps, each owning output rows w, w + W, ... (W =
+// warps of the grid, sized to what is resident). A warp loads up to GV_U 16-byte chunks per lane
+// of its row at once (8 KB of one row per warp in flight) with streaming loads that bypass L1
+// and are marked evict-first in L2, then runs the reference's FMA chain over them. The first
+// batch of a warp's first row is loaded before the programmatic-dependency wait, because weights
+// never depend on the previous kernel, and the next row's first batch is loaded before the
+// current row's reduction and store. x is read through L1, where every warp of the SM finds it.
 #include <algorithm>
 
 #include "common.cuh"
@@ -22,10 +23,10 @@ namespace {
 
 __device__ unsigned g_dev_error;
 
-constexpr int WARPS = 8;                  // consumer warps; one output row each per group
-constexpr int THREADS = (WARPS + 1) * 32;  // + one producer warp
-constexpr int STAGES = 4;
-constexpr int STAGE_TARGET_BYTES = 16384;
+constexpr int GV_THREADS = 256;  // 8 warps per CTA
+// UR: chunk rounds (one 16-byte chunk per lane each) per batch and row; a unit's batch holds
+// RPU * UR chunks per lane. The host picks the smallest UR in {8, 12, 16} that covers a row in
+// one batch, else 16 (8 for gate_up, whose batches hold two rows).
 
 enum Epi : int { PLAIN = 0, RESIDUAL = 1, QKV = 2, GATE_UP = 3 };
 
@@ -37,9 +38,6 @@ struct GemvArgs {
     int rows0, rows1;          // QKV: q_rows, kv_rows
     int units;                 // output rows
     int cols;
-    int seg_cols;              // columns per stage segment (a multiple of 256, or cols)
-    int n_seg;
-    int x_bytes;               // shared bytes reserved for x (cols * 2 rounded up)
 };
 
 template <int EPI>
@@ -54,118 +52,76 @@ __device__ __forceinline__ const bf16 *unit_row(const GemvArgs &a, int u, int r)
     return a.w0 + (size_t)u * a.cols;
 }
 
-template <int EPI>
-__global__ void __launch_bounds__(THREADS, 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
-    constexpr int RPU = EPI == GATE_UP ? 2 : 1;
-    extern __shared__ __align__(128) unsigned char smem[];
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-    uint64_t *empty = full + STAGES;
-    bf16 *x_s = reinterpret_cast<bf16 *>(smem + 128);
-    unsigned char *stages = smem + 128 + a.x_bytes;
-    const size_t row_stride = (size_t)a.seg_cols * 2;  // bytes per row slot in a stage
-    const size_t stage_bytes = (size_t)WARPS * RPU * row_stride;
+// 16-byte streaming load: no L1 allocation, evict-first in L2.
+__device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p), "l"(policy));
+    return v;
+}
 
-    const int warp = threadIdx.x / 32;
+template <int EPI, int UR>
+__global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    constexpr int RPU = EPI == GATE_UP ? 2 : 1;  // weight rows per output unit
     const int lane = threadIdx.x % 32;
-    const int u0 = (int)(((long long)a.units * blockIdx.x) / gridDim.x);
-    const int u1 = (int)(((long long)a.units * (blockIdx.x + 1)) / gridDim.x);
-    const int nu = u1 - u0;
-    const int n_groups = (nu + WARPS - 1) / WARPS;
-    const int n_items = n_groups * a.n_seg;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], WARPS);
-        }
-        fence_barrier_init();
-    }
-    __syncthreads();
-    pdl_trigger();
-
-    if (warp == WARPS) {
-        // ---------------- producer: weights only, so it may run ahead of pdl_wait()
-        if (lane == 0) {
-            const uint64_t policy = policy_evict_first();
-            int it = 0;
-            for (; it < n_items; it++) {
-                const int slot = it % STAGES;
-                if (it >= STAGES && !mbar_wait(&empty[slot], ((it / STAGES) - 1) & 1, &g_dev_error))
-                    break;
-                const int g = it / a.n_seg;
-                const int s = it - g * a.n_seg;
-                const int c0 = s * a.seg_cols;
-                const uint32_t row_bytes = (uint32_t)min(a.seg_cols, a.cols - c0) * 2;
-                const int gu = min(WARPS, nu - g * WARPS);
-                mbar_arrive_expect_tx(&full[slot], (uint32_t)(gu * RPU) * row_bytes);
-                unsigned char *st = stages + slot * stage_bytes;
-                for (int w = 0; w < gu; w++) {
-                    const int u = u0 + g * WARPS + w;
+    const int nw = gridDim.x * (GV_THREADS / 32);
+    const int n_vec = a.cols / 8;
+    const uint64_t policy = policy_evict_first();
+    uint4 w[RPU][UR];
+    // rounds r0 .. r0 + UR - 1 of unit u: chunk lane + 32 * round of each of its rows
+    auto load_batch = [&](int u, int r0) {
 #pragma unroll
-                    for (int r = 0; r < RPU; r++)
-                        bulk_g2s_hint(st + (w * RPU + r) * row_stride, unit_row<EPI>(a, u, r) + c0,
-                                      row_bytes, &full[slot], policy);
-                }
+        for (int r = 0; r < RPU; r++) {
+            const uint4 *row = reinterpret_cast<const uint4 *>(unit_row<EPI>(a, u, r));
+#pragma unroll
+            for (int j = 0; j < UR; j++) {
+                const int i = lane + 32 * (r0 + j);
+                if (i < n_vec) w[r][j] = ldg_stream(row + i, policy);
             }
-            // Do not leave while copies issued into this CTA's shared memory may be in flight.
-            for (int j = max(0, it - STAGES); j < it; j++)
-                mbar_wait(&full[j % STAGES], (j / STAGES) & 1, &g_dev_error);
         }
-        return;
-    }
+    };
 
-    // ---------------- consumers
+    int u = blockIdx.x * (GV_THREADS / 32) + threadIdx.x / 32;
+    pdl_trigger();
+    if (u < a.units) load_batch(u, 0);
     pdl_wait();
-    {
-        const int n8 = a.cols / 8;
-        const uint4 *xg = reinterpret_cast<const uint4 *>(a.x);
-        uint4 *xs = reinterpret_cast<uint4 *>(x_s);
-        for (int i = threadIdx.x; i < n8; i += WARPS * 32) xs[i] = xg[i];
-    }
-    asm volatile("bar.sync 1, %0;" ::"r"(WARPS * 32) : "memory");
-
-    for (int g = 0; g < n_groups; g++) {
-        const int u = u0 + g * WARPS + warp;
-        const bool active = u < u1;
-        float acc0 = 0.0f, acc1 = 0.0f;
-        for (int s = 0; s < a.n_seg; s++) {
-            const int it = g * a.n_seg + s;
-            const int slot = it % STAGES;
-            if (!mbar_wait(&full[slot], (it / STAGES) & 1, &g_dev_error)) return;
-            if (active) {
-                const int c0 = s * a.seg_cols;
-                const int nchunk = min(a.seg_cols, a.cols - c0) / 8;
-                const unsigned char *row0 = stages + slot * stage_bytes + (warp * RPU) * row_stride;
-                const bf16 *xs = x_s + c0;
-                for (int i = lane; i < nchunk; i += 32) {
-                    const bf16x8 xv = lds128(xs + i * 8);
-                    acc0 = dot8(lds128(row0 + i * 16), xv, acc0);
-                    if (EPI == GATE_UP) acc1 = dot8(lds128(row0 + row_stride + i * 16), xv, acc1);
+    const uint4 *xv = reinterpret_cast<const uint4 *>(a.x);
+    for (; u < a.units; u += nw) {
+        float acc[RPU];
+#pragma unroll
+        for (int r = 0; r < RPU; r++) acc[r] = 0.0f;
+        for (int r0 = 0; 32 * r0 < n_vec; r0 += UR) {
+            if (r0 > 0) load_batch(u, r0);
+#pragma unroll
+            for (int j = 0; j < UR; j++) {
+                const int i = lane + 32 * (r0 + j);
+                if (i < n_vec) {
+                    const bf16x8 xc = ldg128(xv + i);
+#pragma unroll
+                    for (int r = 0; r < RPU; r++) acc[r] = dot8(*reinterpret_cast<const bf16x8 *>(&w[r][j]), xc, acc[r]);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        if (!active) continue;
-        for (int off = 16; off > 0; off >>= 1) {
-            acc0 += __shfl_down_sync(0xffffffffu, acc0, off);
-            if (EPI == GATE_UP) acc1 += __shfl_down_sync(0xffffffffu, acc1, off);
-        }
+        if (u + nw < a.units) load_batch(u + nw, 0);  // in flight during the reduction and store
+#pragma unroll
+        for (int r = 0; r < RPU; r++)
+            for (int off = 16; off > 0; off >>= 1) acc[r] += __shfl_down_sync(0xffffffffu, acc[r], off);
         if (lane != 0) continue;
         if (EPI == PLAIN) {
-            a.out0[u] = __float2bfloat16(acc0);
+            a.out0[u] = __float2bfloat16(acc[0]);
         } else if (EPI == RESIDUAL) {
-            const bf16 y = __float2bfloat16(acc0);
+            const bf16 y = __float2bfloat16(acc[0]);
             if (a.tap0 != nullptr) a.tap0[u] = y;
             a.out0[u] = __float2bfloat16(__bfloat162float(a.out0[u]) + __bfloat162float(y));
         } else if (EPI == QKV) {
-            const bf16 y = __float2bfloat16(acc0);
+            const bf16 y = __float2bfloat16(acc[0]);
             if (u < a.rows0) a.out0[u] = y;
             else if (u < a.rows0 + a.rows1) a.out1[u - a.rows0] = y;
             else a.out2[u - a.rows0 - a.rows1] = y;
         } else {
-            const bf16 gate = __float2bfloat16(acc0);
-            const bf16 up = __float2bfloat16(acc1);
+            const bf16 gate = __float2bfloat16(acc[0]);
+            const bf16 up = __float2bfloat16(acc[RPU - 1]);
             if (a.tap0 != nullptr) {
                 a.tap0[u] = gate;
                 a.tap1[u] = up;
@@ -180,22 +136,34 @@ __global__ void __launch_bounds__(THREADS, 1) gemv_kernel(const __grid_constant_
 
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+template <int EPI, int UR>
+int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
+    static int per_sm[64] = {};  // resident CTAs per SM, by device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return Q3_ERR_DEVICE;
+    if (per_sm[dev] == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR>, GV_THREADS, 0) != cudaSuccess || n < 1)
+            n = 1;
+        cudaGetLastError();
+        per_sm[dev] = n;
+    }
+    const long long want = (a.units + GV_THREADS / 32 - 1) / (GV_THREADS / 32);
+    const int grid = (int)std::min<long long>(want, (long long)num_sms() * per_sm[dev]);
+    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR>, dim3(grid), dim3(GV_THREADS), 0, stream, 1, a));
+    return Q3_OK;
+}
+
 template <int EPI>
 int launch_gemv(GemvArgs a, cudaStream_t stream) {
-    constexpr int RPU = EPI == GATE_UP ? 2 : 1;
     if (a.units <= 0 || a.cols <= 0) return a.units == 0 ? Q3_OK : Q3_ERR_SHAPE;
     if (a.cols % 8 != 0) return Q3_ERR_SHAPE;
-    int seg = (STAGE_TARGET_BYTES / (WARPS * RPU * 2)) / 256 * 256;
-    seg = std::max(seg, 256);
-    a.seg_cols = a.cols <= seg ? a.cols : seg;
-    a.n_seg = (a.cols + a.seg_cols - 1) / a.seg_cols;
-    a.x_bytes = (a.cols * 2 + 127) / 128 * 128;
-    const size_t smem = 128 + (size_t)a.x_bytes + (size_t)STAGES * WARPS * RPU * a.seg_cols * 2;
-    if (smem > 227 * 1024) return Q3_ERR_SHAPE;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(gemv_kernel<EPI>), smem));
-    const int grid = std::min(num_sms(), a.units);
-    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
-    return Q3_OK;
+    const int rounds = (a.cols / 8 + 31) / 32;
+    if (rounds <= 8) return launch_gemv_ur<EPI, 8>(a, stream);
+    if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
+    if constexpr (EPI == GATE_UP) return launch_gemv_ur<EPI, 8>(a, stream);  // two rows: 16 chunks a batch
+    else return launch_gemv_ur<EPI, 16>(a, stream);
 }
 
 }  // namespace

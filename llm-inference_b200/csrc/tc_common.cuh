@@ -101,6 +101,21 @@ inline bool make_map_strided(CUtensorMap *map, const void *base, long long rows,
     return r == CUDA_SUCCESS;
 }
 
+// 2-D bf16 map without swizzle and a [box_rows, box_cols] box (box_cols * 2 a multiple of 16).
+inline bool make_map_plain(CUtensorMap *map, const void *base, long long rows, long long cols, long long row_stride,
+                           int box_rows, int box_cols) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+    cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
 inline bool make_map(CUtensorMap *map, const void *base, int rows, int cols, int box_rows) {
     return make_map_strided(map, base, rows, cols, cols, box_rows);
 }
