@@ -118,6 +118,11 @@ class ClockSampler:
 # ---------------------------------------------------------------- distributed plumbing
 
 class Dist:
+    """One process per GPU (RANK / LOCAL_RANK / WORLD_SIZE from torch.distributed.run). The process
+    group only brackets the timed regions and takes the maximum time over ranks: decode sequences
+    are independent, so nothing is exchanged on the decode path. NCCL on GPUs; gloo on a host
+    without CUDA (the CPU tests of this plumbing)."""
+
     def __init__(self, n_gpus: int):
         import torch
         self.world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -125,12 +130,18 @@ class Dist:
         self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
         if self.world != n_gpus:
             raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}: launch N>1 with torch.distributed.run")
-        torch.cuda.set_device(self.local_rank)
+        cuda = torch.cuda.is_available()
+        if cuda:
+            torch.cuda.set_device(self.local_rank)
+        self.device = "cuda" if cuda else "cpu"
         self.pg = None
         if self.world > 1:
             import torch.distributed as dist
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                    device_id=torch.device("cuda", self.local_rank))
+            if cuda:
+                dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                        device_id=torch.device("cuda", self.local_rank))
+            else:
+                dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=60))
             self.pg = dist
 
     def barrier(self):
@@ -141,13 +152,14 @@ class Dist:
         if not self.pg:
             return value
         import torch
-        t = torch.tensor([value], dtype=torch.float64, device="cuda")
+        t = torch.tensor([value], dtype=torch.float64, device=self.device)
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
     def close(self):
         if self.pg:
             self.pg.destroy_process_group()
+            self.pg = None
 
 
 def timed(dist, stream, fn, name: str) -> float:
