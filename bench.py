@@ -40,6 +40,7 @@ MODEL = "qwen3-4b"
 BATCH_PER_GPU = 32
 KV_PREFILL = 4096
 METRIC = "decode tok/s (Qwen3-4B, 32 seq/GPU, KV 4096, greedy)"
+ATTN_TRAFFIC_BYTES = 591_933_696  # measured DRAM bytes of one attention launch (ncu)
 
 
 def _package():
@@ -313,7 +314,83 @@ def kernel_roofline(eng, stream, hbm_peak, measured) -> dict:
     return {"kernel": "attention (q3_attention_batched: scores + pv kernels), one layer, 32 sequences",
             "bound": "hbm", "achieved": round(gbs, 1), "peak": hbm_peak, "unit": "GB/s", "frac": round(gbs / hbm_peak, 4),
             "algorithmic_bytes_per_launch": int(alg), "us_per_launch": round(ms * 1e3, 2),
-            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if measured else "fallback", "traffic": None}
+            "peak_source": "MEASURED_PEAKS.json hbm_gbs" if measured else "fallback",
+            # dram__bytes_read.sum + dram__bytes_write.sum of the four attention kernels of one
+            # launch at this exact shape, from an ncu capture
+            "traffic": ATTN_TRAFFIC_BYTES, "traffic_source": "ncu capture, one launch at position 4095"}
+
+
+def run_config3(args) -> dict | None:
+    """Qwen3-4B at batch 1, greedy decode, tok/s at positions 256, 2048
+    and 8192 (the cache before each position pre-filled with bf16 N(0, 1), standing in for the
+    tokens a real decode would have written). One engine, one captured step, replayed K times at
+    each position; `value` is the rate at position 2048 and `e2e` the per-token host protocol
+    there. Per-token algorithmic bytes: all weights plus the KV rows of every position attended."""
+    import torch
+    q3 = _package()
+    from llm_inference_b200 import checkpoint
+    from llm_inference_b200.engine import DeviceWeights, Engine
+    if args.gpus != 1:
+        raise SystemExit("--workload config3 runs on one GPU")
+    dist = Dist(1)
+    shape = checkpoint.PRESETS[MODEL]
+    K, W = args.steps, args.warmup
+    positions = (256, 2048, 8192)
+    max_seq = max(positions) + W + 2 * K + 16
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        weights = DeviceWeights.random(shape, seed=0)
+        eng = Engine(weights, batch=1, max_seq=max_seq, history_cap=4 * (W + K) + 8, stream=stream.cuda_stream)
+        eng.capture()
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    per_pos, e2e = {}, None
+    weight_bytes, kvpp = eng.weight_bytes_per_step(), eng.kv_bytes_per_position()
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        for p in positions:
+            eng.fill_kv_normal(p, seed=1000 + p)
+            eng.set_state([17], [p])
+            eng.step(W)
+            ms = timed(dist, stream.cuda_stream, lambda: eng.step(K), "decode_steps")
+            tok_s = K / (ms * 1e-3)
+            step_bytes = weight_bytes + kvpp * (p + W + (K + 1) / 2)
+            gbs = step_bytes * tok_s / 1e9
+            per_pos[str(p)] = {"tok_s": round(tok_s, 1), "ms_per_token": round(ms / K, 4),
+                               "bytes_per_token": int(step_bytes), "achieved_gbs": round(gbs, 1),
+                               "frac": round(gbs / hbm, 4)}
+            if p == 2048:
+                toks = eng.sample_argmax()
+                pos0 = p + W + K
+                def e2e_fn():
+                    t = toks
+                    for i in range(K):
+                        eng.forward(t, [pos0 + i])
+                        t = eng.sample_argmax()
+                ms_e2e = timed(dist, stream.cuda_stream, e2e_fn, "decode_e2e")
+                e2e = {"value": round(K / (ms_e2e * 1e-3), 1), "unit": "tok/s", "h2d_bytes_per_step": 8,
+                       "d2h_bytes_per_step": 4}
+    clocks = clk.summary()
+    if q3.device_error(stream.cuda_stream) != 0:
+        raise SystemExit("device error flags set during the benchmark")
+    mid = per_pos["2048"]
+    line = {"metric": "decode tok/s (Qwen3-4B, batch 1, greedy) at positions 256/2048/8192", "value": mid["tok_s"],
+            "unit": "tok/s", "n_gpus": 1, "steps": K, "warmup": W, "ms_per_step": mid["ms_per_token"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, N(0,1) KV before each position)",
+            "config": {"workload": "BASELINE config 3: Qwen3-4B random-init, batch 1, greedy decode, rates at "
+                                   "positions 256, 2048 and 8192", "model": MODEL, "global_batch": 1,
+                       "parallelism": "dp1", "l2": "no flush: 8.0 GB of weights per token exceed the 126 MB L2"},
+            "positions": per_pos, "clocks": clocks, "e2e": e2e, "gpu_launches": eng.launches_per_step() * K,
+            "step_roofline": {"bound": "hbm", "bytes_per_step": mid["bytes_per_token"], "achieved": mid["achieved_gbs"],
+                              "peak": hbm, "unit": "GB/s", "frac": mid["frac"],
+                              "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"}}
+    eng.close()
+    dist.close()
+    return line
 
 
 def run_reference(args) -> dict | None:
@@ -349,11 +426,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--workload", choices=["config4", "config3"], default="config4",
+                    help="config4 (default): 32 sequences per GPU at KV 4096; config3: batch 1 at 256/2048/8192")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         line = run_reference(args)
+    elif args.workload == "config3":
+        line = run_config3(args)
     else:
         line = run_mine(args)
         if line is not None and args.gpus == 1 and not args.no_cpu_baseline:
