@@ -276,6 +276,15 @@ int q3_engine_set_state(q3_engine *e, const int *tokens, const int *positions);
 int q3_engine_forward(q3_engine *e, const int *tokens, const int *positions);
 int q3_engine_sample_argmax(q3_engine *e, int *tokens_out);
 
+/* Prefill (the reference feeds a prompt one token per forward, src/main.cu:122-124): runs the
+ * n_tokens host token ids of sequence `seq` at positions start_pos .. start_pos + n_tokens - 1
+ * through the layers, up to `batch` tokens per pass. The rows of a pass share the sequence's
+ * cache and attend causally (row i sees positions up to its own). Their K and V rows are written
+ * to the cache. next_token[seq] / out_token[seq] become the argmax of the last token's logits and
+ * pos[seq] becomes start_pos + n_tokens, so decode steps continue from there. Other sequences'
+ * caches and state are left as they were; the logits buffer is overwritten. Waits for its work. */
+int q3_engine_prefill(q3_engine *e, int seq, const int *tokens, int n_tokens, int start_pos);
+
 /* Fills cache positions [0, n_positions) of every layer and sequence with bf16 N(0,1). */
 int q3_engine_fill_kv_normal(q3_engine *e, int n_positions, unsigned long long seed);
 

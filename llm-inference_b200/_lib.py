@@ -59,6 +59,7 @@ SIGNATURES: dict[str, list] = {
     "q3_engine_set_state": [_P, _P, _P],
     "q3_engine_forward": [_P, _P, _P],
     "q3_engine_sample_argmax": [_P, _P],
+    "q3_engine_prefill": [_P, _I, _P, _I, _I],
     "q3_engine_fill_kv_normal": [_P, _I, ctypes.c_ulonglong],
     "q3_engine_info": [_P, _P],
 }

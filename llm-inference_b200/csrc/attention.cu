@@ -462,7 +462,10 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 // ------------------------------------------------------------------ scores on tcgen05 (split mode)
 constexpr int TC_TILE = 128;        // positions per item = MMA M
 constexpr int TC_N = 16;            // MMA N: query heads of the group, padded
-constexpr int TC_STAGES = 4;
+#ifndef Q3_SCORES_STAGES
+#define Q3_SCORES_STAGES 4
+#endif
+constexpr int TC_STAGES = Q3_SCORES_STAGES;
 constexpr int TC_ACC = 4;           // TMEM accumulators (TC_N columns each)
 constexpr int TC_THREADS = 192;     // producer warp, MMA warp, 4 epilogue warps
 
@@ -603,7 +606,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 // fp32 additions differs from a serial chain. V rows past the end of the sequence are zeroed in
 // shared memory before the MMA (the cache there may hold anything, and 0 * NaN is NaN).
 constexpr int PV_TILE = 128;
-constexpr int PV_STAGES = 4;
+#ifndef Q3_PV_STAGES
+#define Q3_PV_STAGES 4
+#endif
+constexpr int PV_STAGES = Q3_PV_STAGES;
 constexpr int PV_ACC = 2;
 constexpr int PV_V_BYTES = PV_TILE * 128;      // one 64-dim half of a V tile
 constexpr int PV_P_OFF = 2 * PV_V_BYTES;       // P: 2 swizzle atoms of 16 rows x 128 B
@@ -969,6 +975,14 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const __grid_constant
     }
 }
 
+// Rows of the [rows, kv.pos] view of a K or V cache that the TMA maps cover: every sequence's
+// rows, or, when all rows share one cache (sequence stride 0: the rows of one prompt), that
+// cache's rows (n_kv heads of max_seq positions head-major, or max_seq positions).
+long long cache_map_rows(const AttnArgs &a) {
+    if (a.kv.seq > 0) return (long long)a.B * (a.kv.seq / a.kv.pos);
+    return a.kv.head >= a.kv.pos ? (long long)a.n_kv * (a.kv.head / a.kv.pos) : (long long)a.max_seq;
+}
+
 template <int NREP>
 int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     ScoreTcPlan pl;
@@ -980,7 +994,7 @@ int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     // kind::f16: fp32 accumulate, bf16 A and B, both K-major, N = 16, M = 128
     pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_TILE >> 4) << 24);
     CUtensorMap mk, mq;
-    if (!make_map_strided(&mk, a.kc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, TC_TILE)) return Q3_ERR_ARG;
+    if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, TC_TILE)) return Q3_ERR_ARG;
     if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TC_N)) return Q3_ERR_ARG;
     const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)PREFIX_INTS(a.B) * 4;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_tc_kernel<NREP>), smem));
@@ -1012,7 +1026,7 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
     pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) |
                ((uint32_t)(128 >> 4) << 24);
     CUtensorMap mv;
-    if (!make_map_strided(&mv, a.vc, (long long)a.B * pl.k_rows_per_seq, a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
+    if (!make_map_strided(&mv, a.vc, cache_map_rows(a), a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
     const size_t smem = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)PREFIX_INTS(a.B) * 4;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);

@@ -20,6 +20,8 @@
 
 #include <vector>
 
+#include <algorithm>
+
 #include "common.cuh"
 
 namespace q3 {
@@ -68,6 +70,7 @@ struct q3_engine {
     AttnSplit split;
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
+    int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
     int *host_io;  // pinned: [2B] for token/position uploads, [B] for downloads
     cudaGraphExec_t graph;
     int graph_kernels;  // kernel nodes of the captured step
@@ -90,36 +93,48 @@ int alloc(q3_engine *e, void **p, size_t bytes) {
         if (st_ != Q3_OK) return st_; \
     } while (0)
 
-int enqueue_step(q3_engine *e) {
+// The decoder layers for `rows` rows of activations. Row b reads its token id and position from
+// tok[b] / pos[b]; its KV rows go to the cache of sequence (cache_seq + b), or, when
+// shared_cache, every row's to the cache of sequence cache_seq (one prompt's chunk at
+// consecutive positions: row b attends positions 0..pos[b] of that cache, so the chunk is causal).
+int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int cache_seq, bool shared_cache) {
     const q3_config &c = e->cfg;
     const int B = e->B, H = c.hidden_size, I = c.intermediate_size;
     const int qd = c.n_heads * c.head_dim, kvd = c.n_kv_heads * c.head_dim;
     const long long seq_stride = (long long)e->max_seq * kvd;  // one (layer, sequence): n_kv heads x max_seq rows
-    const KvLayout kv = {seq_stride, c.head_dim, (long long)e->max_seq * c.head_dim};
+    const KvLayout kv = {shared_cache ? 0 : seq_stride, c.head_dim, (long long)e->max_seq * c.head_dim};
     const float scale = (float)(1.0 / sqrt((double)c.head_dim));
     cudaStream_t s = e->stream;
     const bool exact_attn = (e->flags & Q3_ENGINE_EXACT_ATTENTION) != 0;
 
-    TRY(embedding(e->x, e->embed, e->next_token, B, H, c.vocab_size, s));
+    TRY(embedding(e->x, e->embed, tok, rows, H, c.vocab_size, s));
     for (int l = 0; l < c.n_layers; l++) {
         const q3_layer_weights &w = e->layers[l];
-        bf16 *kc = e->key_cache + (size_t)l * B * seq_stride;
-        bf16 *vc = e->value_cache + (size_t)l * B * seq_stride;
-        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.attn_norm, B, H, c.rms_norm_eps, s));
-        TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, B, qd, kvd,
-                     H, s));
-        TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, e->pos, B, qd,
+        bf16 *kc = e->key_cache + ((size_t)l * B + cache_seq) * seq_stride;
+        bf16 *vc = e->value_cache + ((size_t)l * B + cache_seq) * seq_stride;
+        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.attn_norm, rows, H, c.rms_norm_eps, s));
+        TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, rows, qd,
+                     kvd, H, s));
+        TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, pos, rows, qd,
                          kvd, kv, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps, c.rope_theta,
                          nullptr, nullptr, s));
-        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), e->pos, B, qd, kv, c.n_heads,
+        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), pos, rows, qd, kv, c.n_heads,
                       c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
-        TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, B, H, qd, nullptr, s));
-        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, B, H, c.rms_norm_eps, s));
-        TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, B, I, H, nullptr, nullptr, s));
-        TRY(proj_residual(e->x, (const bf16 *)w.w_down, e->hb, B, H, I, nullptr, s));
+        TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, rows, H, qd, nullptr, s));
+        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, rows, H, c.rms_norm_eps, s));
+        TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, rows, I, H, nullptr, nullptr, s));
+        TRY(proj_residual(e->x, (const bf16 *)w.w_down, e->hb, rows, H, I, nullptr, s));
     }
-    TRY(rmsnorm(e->xb, e->x, e->final_norm, B, H, c.rms_norm_eps, s));
-    TRY(proj(e->logits, e->lm_head, e->xb, B, c.vocab_size, H, s));
+    TRY(rmsnorm(e->xb, e->x, e->final_norm, rows, H, c.rms_norm_eps, s));
+    TRY(proj(e->logits, e->lm_head, e->xb, rows, c.vocab_size, H, s));
+    return Q3_OK;
+}
+
+int enqueue_step(q3_engine *e) {
+    const q3_config &c = e->cfg;
+    const int B = e->B;
+    cudaStream_t s = e->stream;
+    TRY(enqueue_layers(e, B, e->next_token, e->pos, 0, false));
     TRY(argmax_rows(e->logits, c.vocab_size, B, c.vocab_size, e->out_token, e->next_token, e->pos, e->history,
                     e->step, e->history_cap, s));
     return Q3_OK;
@@ -207,6 +222,8 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->out_token, B * 4);
     A((void **)&e->history, (size_t)(history_cap > 0 ? history_cap : 1) * B * 4);
     A((void **)&e->step, 16);
+    A((void **)&e->pf_token, B * 4);
+    A((void **)&e->pf_pos, B * 4);
     if (r == Q3_OK) r = record_cuda_error(cudaMallocHost((void **)&e->host_io, 3 * B * sizeof(int)));
     if (r != Q3_OK) {
         release(e);
@@ -302,6 +319,41 @@ int q3_engine_set_state(q3_engine *e, const int *tokens, const int *positions) {
 int q3_engine_forward(q3_engine *e, const int *tokens, const int *positions) {
     int r = q3_engine_set_state(e, tokens, positions);
     return r == Q3_OK ? q3_engine_step(e, 1) : r;
+}
+
+int q3_engine_prefill(q3_engine *e, int seq, const int *tokens, int n_tokens, int start_pos) {
+    if (!e || !tokens) return Q3_ERR_ARG;
+    if (seq < 0 || seq >= e->B || n_tokens <= 0 || start_pos < 0 || (long long)start_pos + n_tokens > e->max_seq)
+        return Q3_ERR_SHAPE;
+    for (int i = 0; i < n_tokens; i++)
+        if (tokens[i] < 0 || tokens[i] >= e->cfg.vocab_size) return Q3_ERR_SHAPE;
+    const int V = e->cfg.vocab_size;
+    int *io = e->host_io;
+    int rows = 0;
+    for (int c0 = 0; c0 < n_tokens; c0 += e->B) {
+        rows = std::min(e->B, n_tokens - c0);
+        int r = record_cuda_error(cudaStreamSynchronize(e->stream));  // the pinned staging buffer is reused
+        if (r != Q3_OK) return r;
+        for (int i = 0; i < rows; i++) {
+            io[i] = tokens[c0 + i];
+            io[e->B + i] = start_pos + c0 + i;
+        }
+        r = record_cuda_error(cudaMemcpyAsync(e->pf_token, io, rows * sizeof(int), cudaMemcpyHostToDevice, e->stream));
+        if (r == Q3_OK)
+            r = record_cuda_error(cudaMemcpyAsync(e->pf_pos, io + e->B, rows * sizeof(int), cudaMemcpyHostToDevice,
+                                                  e->stream));
+        if (r != Q3_OK) return r;
+        TRY(enqueue_layers(e, rows, e->pf_token, e->pf_pos, seq, true));
+    }
+    // the prompt's last token: its logits give the sequence's next token; its position follows
+    TRY(argmax_rows(e->logits + (size_t)(rows - 1) * V, V, 1, V, e->out_token + seq, e->next_token + seq, nullptr,
+                    nullptr, nullptr, 0, e->stream));
+    int r = record_cuda_error(cudaStreamSynchronize(e->stream));
+    if (r != Q3_OK) return r;
+    io[2 * e->B] = start_pos + n_tokens;
+    r = record_cuda_error(cudaMemcpyAsync(e->pos + seq, io + 2 * e->B, sizeof(int), cudaMemcpyHostToDevice, e->stream));
+    if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(e->stream));
+    return r;
 }
 
 int q3_engine_sample_argmax(q3_engine *e, int *tokens_out) {

@@ -59,7 +59,10 @@ constexpr int EPI_THREADS = 128;
 constexpr int BK = 64;            // K per stage: 64 bf16 = one 128-byte swizzle row
 constexpr int TILE_M = 128;       // MMA M
 constexpr int MAX_STAGES = 12;
-constexpr int KSUB = 4;           // 64-column sub-tiles per stage: 512 contiguous bytes per weight row
+#ifndef Q3_GEMM_KSUB
+#define Q3_GEMM_KSUB 4
+#endif
+constexpr int KSUB = Q3_GEMM_KSUB;  // 64-column sub-tiles per stage: 512 contiguous bytes per weight row
 #ifndef Q3_GEMM_SMEM_BUDGET_KB
 #define Q3_GEMM_SMEM_BUDGET_KB 112  // leaves room for a co-resident successor kernel
 #endif

@@ -162,6 +162,12 @@ class Engine:
         p = (ctypes.c_int * self.batch)(*[int(v) for v in positions])
         call("q3_engine_forward", self.handle, t, p)
 
+    def prefill(self, seq: int, tokens, start_pos: int = 0):
+        """Runs sequence `seq`'s prompt `tokens` from `start_pos` in passes of up to `batch` tokens;
+        afterwards its next token is the argmax after the prompt and its position follows it."""
+        t = (ctypes.c_int * len(tokens))(*[int(v) for v in tokens])
+        call("q3_engine_prefill", self.handle, int(seq), t, len(tokens), int(start_pos))
+
     def sample_argmax(self) -> list[int]:
         out = (ctypes.c_int * self.batch)()
         call("q3_engine_sample_argmax", self.handle, out)
