@@ -340,7 +340,8 @@ def run_config3(args) -> dict | None:
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         weights = DeviceWeights.random(shape, seed=0)
-        eng = Engine(weights, batch=1, max_seq=max_seq, history_cap=4 * (W + K) + 8, stream=stream.cuda_stream)
+        eng = Engine(weights, batch=1, max_seq=max_seq, history_cap=4 * (W + K) + 8, stream=stream.cuda_stream,
+                     megakernel=args.megakernel)
         eng.capture()
     peaks = {}
     try:
@@ -383,7 +384,9 @@ def run_config3(args) -> dict | None:
             "data": "synthetic (random-init weights, N(0,1) KV before each position)",
             "config": {"workload": "BASELINE config 3: Qwen3-4B random-init, batch 1, greedy decode, rates at "
                                    "positions 256, 2048 and 8192", "model": MODEL, "global_batch": 1,
-                       "parallelism": "dp1", "l2": "no flush: 8.0 GB of weights per token exceed the 126 MB L2"},
+                       "parallelism": "dp1", "l2": "no flush: 8.0 GB of weights per token exceed the 126 MB L2",
+                       "path": "one persistent cooperative kernel per token" if args.megakernel
+                       else "captured graph of per-op kernels"},
             "positions": per_pos, "clocks": clocks, "e2e": e2e, "gpu_launches": eng.launches_per_step() * K,
             "step_roofline": {"bound": "hbm", "bytes_per_step": mid["bytes_per_token"], "achieved": mid["achieved_gbs"],
                               "peak": hbm, "unit": "GB/s", "frac": mid["frac"],
@@ -426,6 +429,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["mine", "reference"], default="mine")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--megakernel", action="store_true",
+                    help="config3: run each token as one persistent cooperative kernel (Q3_ENGINE_MEGAKERNEL)")
     ap.add_argument("--workload", choices=["config4", "config3"], default="config4",
                     help="config4 (default): 32 sequences per GPU at KV 4096; config3: batch 1 at 256/2048/8192")
     args = ap.parse_args()

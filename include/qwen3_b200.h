@@ -247,7 +247,13 @@ typedef struct q3_engine_buffers {
     int launches_per_step; /* kernel launches in the captured step (0 before q3_engine_capture) */
 } q3_engine_buffers;
 
-enum { Q3_ENGINE_EXACT_ATTENTION = 1 /* bit-exact single-chunk attention instead of split-KV */ };
+enum {
+    Q3_ENGINE_EXACT_ATTENTION = 1, /* bit-exact single-chunk attention instead of split-KV */
+    /* batch 1 only: each step is one cooperative kernel whose CTAs pass through the step's phases
+     * (norms, projections, RoPE, attention, LM head, argmax) separated by grid barriers, instead
+     * of ~290 kernels; per-row arithmetic as in the other path, P.V summed in 128-position parts */
+    Q3_ENGINE_MEGAKERNEL = 2
+};
 
 /* src/forward.cu:83-114 weight_bytes_per_step and kv_bytes_per_position. */
 size_t q3_weight_bytes_per_step(const q3_config *cfg);

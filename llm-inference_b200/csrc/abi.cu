@@ -32,6 +32,7 @@ unsigned take_error_gemv();
 unsigned take_error_decode();
 unsigned take_error_attention();
 unsigned take_error_tc();
+unsigned take_error_megakernel();
 
 namespace {
 constexpr int MAX_DEVICES = 64;
@@ -135,7 +136,8 @@ int q3_device_error(void *stream, unsigned *flags) {
     if (!flags) return Q3_ERR_ARG;
     cudaError_t e = cudaStreamSynchronize(S(stream));
     if (e != cudaSuccess) return q3::record_cuda_error(e);
-    *flags = q3::take_error_gemv() | q3::take_error_decode() | q3::take_error_attention() | q3::take_error_tc();
+    *flags = q3::take_error_gemv() | q3::take_error_decode() | q3::take_error_attention() | q3::take_error_tc() |
+             q3::take_error_megakernel();
     return Q3_OK;
 }
 

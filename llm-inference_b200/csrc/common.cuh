@@ -198,6 +198,35 @@ struct KvLayout {
 
 // Scratch of the split-KV attention (attention.cu): softmax statistics and per-chunk partial
 // outputs (the counters are unused).
+// Batch-1 persistent decode kernel (megakernel.cu): per-layer weight pointers and the step's
+// buffers, filled by the engine.
+struct MkLayer {
+    const bf16 *attn_norm, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *mlp_norm, *w_gate, *w_up, *w_down;
+};
+
+struct MkParams {
+    const MkLayer *layers;  // device array [n_layers]
+    const bf16 *embed, *final_norm, *lm_head;
+    int n_layers, H, I, n_heads, n_kv, hd, vocab;
+    float eps, theta, scale;
+    bf16 *x, *q, *k, *v, *attn_out, *act, *logits;
+    bf16 *key_cache, *value_cache;  // layer l at + l * layer_stride; [n_kv][max_seq][hd]
+    long long layer_stride;
+    int max_seq;
+    float *scores;   // [n_heads][ld]
+    int ld;
+    float *stats;    // [n_heads][2]
+    float *partial;  // [2 * max_items][n_heads][hd]
+    float *amax_val;  // [gridDim.x]
+    int *amax_idx;
+    int *next_token, *pos, *out_token, *history, *step;
+    int history_cap;
+    unsigned *bar;   // [0] arrivals, [1] generation, [2] error (sticky)
+};
+
+int megakernel_grid(int nrep);
+int megakernel_launch(const MkParams &p, int nrep, int grid, cudaStream_t s);
+
 struct AttnSplit {
     float *stats;
     float *partial;

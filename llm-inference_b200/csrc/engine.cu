@@ -71,6 +71,10 @@ struct q3_engine {
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
     int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
+    // Q3_ENGINE_MEGAKERNEL: the whole step as one cooperative kernel (batch 1)
+    bool mk = false;
+    MkParams mkp = {};
+    int mk_nrep = 0, mk_grid = 0;
     int *host_io;  // pinned: [2B] for token/position uploads, [B] for downloads
     cudaGraphExec_t graph;
     int graph_kernels;  // kernel nodes of the captured step
@@ -131,6 +135,7 @@ int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int c
 }
 
 int enqueue_step(q3_engine *e) {
+    if (e->mk) return megakernel_launch(e->mkp, e->mk_nrep, e->mk_grid, e->stream);
     const q3_config &c = e->cfg;
     const int B = e->B;
     cudaStream_t s = e->stream;
@@ -178,6 +183,10 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
         return Q3_ERR_SHAPE;
     st = attention_check(c.n_heads, c.n_kv_heads, c.head_dim, max_seq, batch);
     if (st != Q3_OK) return st;
+    const bool mk = (flags & Q3_ENGINE_MEGAKERNEL) != 0;
+    if (mk && (batch != 1 || (c.head_dim != 64 && c.head_dim != 128) || c.hidden_size > 8192 ||
+               ((long long)c.n_heads * c.head_dim) % 8))
+        return Q3_ERR_SHAPE;
     q3_engine *e = new q3_engine();
     e->cfg = c;
     e->layers.assign(w->layers, w->layers + c.n_layers);
@@ -224,6 +233,18 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->step, 16);
     A((void **)&e->pf_token, B * 4);
     A((void **)&e->pf_pos, B * 4);
+    if (mk) {
+        e->mk = true;
+        e->mk_nrep = c.n_heads / c.n_kv_heads;
+        e->mk_grid = megakernel_grid(e->mk_nrep);
+        if (e->mk_grid <= 0 && r == Q3_OK) r = Q3_ERR_DEVICE;
+        const size_t parts = (size_t)((max_seq + 255) / 256) * (256 / c.head_dim);
+        A((void **)&e->mkp.partial, parts * qd * 4);
+        A((void **)&e->mkp.amax_val, (size_t)std::max(e->mk_grid, 1) * 4);
+        A((void **)&e->mkp.amax_idx, (size_t)std::max(e->mk_grid, 1) * 4);
+        A((void **)&e->mkp.bar, 16);
+        A((void **)&e->mkp.layers, (size_t)c.n_layers * sizeof(MkLayer));
+    }
     if (r == Q3_OK) r = record_cuda_error(cudaMallocHost((void **)&e->host_io, 3 * B * sizeof(int)));
     if (r != Q3_OK) {
         release(e);
@@ -238,6 +259,53 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->next_token, 0, B * 4, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->pos, 0, B * 4, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->step, 0, 16, s));
+    if (mk && r == Q3_OK) {
+        std::vector<MkLayer> lw(c.n_layers);
+        for (int l = 0; l < c.n_layers; l++) {
+            const q3_layer_weights &w_ = e->layers[l];
+            lw[l] = {(const bf16 *)w_.attn_norm, (const bf16 *)w_.wq, (const bf16 *)w_.wk, (const bf16 *)w_.wv,
+                     (const bf16 *)w_.q_norm, (const bf16 *)w_.k_norm, (const bf16 *)w_.wo, (const bf16 *)w_.mlp_norm,
+                     (const bf16 *)w_.w_gate, (const bf16 *)w_.w_up, (const bf16 *)w_.w_down};
+        }
+        r = record_cuda_error(cudaMemcpyAsync((void *)e->mkp.layers, lw.data(), lw.size() * sizeof(MkLayer),
+                                              cudaMemcpyHostToDevice, s));
+        if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->mkp.bar, 0, 16, s));
+        if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(s));  // `lw` leaves scope
+        MkParams &p = e->mkp;
+        p.embed = e->embed;
+        p.final_norm = e->final_norm;
+        p.lm_head = e->lm_head;
+        p.n_layers = c.n_layers;
+        p.H = c.hidden_size;
+        p.I = c.intermediate_size;
+        p.n_heads = c.n_heads;
+        p.n_kv = c.n_kv_heads;
+        p.hd = c.head_dim;
+        p.vocab = c.vocab_size;
+        p.eps = c.rms_norm_eps;
+        p.theta = c.rope_theta;
+        p.scale = (float)(1.0 / sqrt((double)c.head_dim));
+        p.x = e->x;
+        p.q = e->q;
+        p.k = e->k;
+        p.v = e->v;
+        p.attn_out = e->attn_out;
+        p.act = e->hb;
+        p.logits = e->logits;
+        p.key_cache = e->key_cache;
+        p.value_cache = e->value_cache;
+        p.layer_stride = (long long)max_seq * kvd;
+        p.max_seq = max_seq;
+        p.scores = e->scores;
+        p.ld = score_ld(max_seq);
+        p.stats = e->split.stats;
+        p.next_token = e->next_token;
+        p.pos = e->pos;
+        p.out_token = e->out_token;
+        p.history = history_cap > 0 ? e->history : nullptr;
+        p.step = e->step;
+        p.history_cap = history_cap;
+    }
     if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(s));
     if (r != Q3_OK) {
         release(e);
@@ -256,6 +324,10 @@ int q3_engine_destroy(q3_engine *e) {
 
 int q3_engine_capture(q3_engine *e) {
     if (!e) return Q3_ERR_ARG;
+    if (e->mk) {  // a step is already one launch
+        e->graph_kernels = 1;
+        return Q3_OK;
+    }
     if (e->graph) {
         cudaGraphExecDestroy(e->graph);
         e->graph = nullptr;
