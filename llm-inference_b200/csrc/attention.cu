@@ -528,6 +528,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer
+        const uint64_t stream_pol = policy_evict_first();  // K rows are read once per step
         int k = 0;
         for (; k < n; k++) {
             const int st = k % TC_STAGES;
@@ -538,7 +539,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * TC_TILE;
             const int qrow = it.b * a.n_heads + it.kvh * NREP;
             for (int h = 0; h < pl.halves; h++) {
-                tma_load_2d(base + h * kbytes, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow, &full[st]);
+                tma_load_2d_stream(base + h * kbytes, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow, &full[st], stream_pol);
                 tma_load_2d(base + pl.halves * kbytes + h * qbytes, &tmQ, h * TMA_BK, qrow, &full[st]);
             }
         }
@@ -679,6 +680,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer: V tile halves by TMA, the group's scores by bulk copy
+        const uint64_t stream_pol = policy_evict_first();  // V rows are read once per step
         int k = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++) {
@@ -703,8 +705,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const bool first = tt == t0;
                 mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + NREP * sbytes + (first ? tbytes : 0));
                 if (first) bulk_g2s(base + PV_T_OFF, reinterpret_cast<const void *>(st_al), tbytes, &full[st]);
-                tma_load_2d(base, &tmV, it.kvh * pl.k_cols_per_head, row0 + tt, &full[st]);
-                tma_load_2d(base + PV_V_BYTES, &tmV, it.kvh * pl.k_cols_per_head + TMA_BK, row0 + tt, &full[st]);
+                tma_load_2d_stream(base, &tmV, it.kvh * pl.k_cols_per_head, row0 + tt, &full[st], stream_pol);
+                tma_load_2d_stream(base + PV_V_BYTES, &tmV, it.kvh * pl.k_cols_per_head + TMA_BK, row0 + tt, &full[st], stream_pol);
 #pragma unroll
                 for (int h = 0; h < NREP; h++)
                     bulk_g2s(base + PV_S_OFF + h * PV_TILE * 4, sc + (size_t)h * a.ld + tt, sbytes, &full[st]);

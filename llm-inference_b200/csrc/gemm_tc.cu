@@ -13,8 +13,9 @@
 //   warp 1, lane 0   MMA issuer: tcgen05.mma kind::f16 (bf16 in, fp32 accumulate) into TMEM,
 //                    tcgen05.commit releases each stage and, after the last K step, the
 //                    accumulator.
-//   warps 2-5        epilogue: tcgen05.ld of the fp32 accumulator rows (one TMEM lane per
-//                    output row; warp w reads lanes 32*(w%4)..+31), then the reference's bf16
+//   warps 2..        epilogue, EPI_GROUPS groups of 4 warps: tcgen05.ld of the fp32 accumulator
+//                    rows (one TMEM lane per output row; warp w reads lanes 32*(w%4)..+31, group
+//                    g every EPI_GROUPS-th chunk of 8 columns from 8g), then the reference's bf16
 //                    rounding points: plain, residual (src/kernels.cu:196-201), q/k/v, or
 //                    SwiGLU (:277-286). The single accumulator is reused tile after tile; the
 //                    producer keeps prefetching the next tile's stages meanwhile.
@@ -54,8 +55,15 @@ namespace {
 
 __device__ unsigned g_dev_error;
 
-constexpr int TC_THREADS = 192;  // producer warp, MMA warp, 4 epilogue warps
-constexpr int EPI_THREADS = 128;
+#ifndef Q3_GEMM_EPI_GROUPS
+#define Q3_GEMM_EPI_GROUPS 2
+#endif
+// Epilogue warp groups. Each group of four warps covers the 128 TMEM lanes once and takes every
+// G-th chunk of 8 accumulator columns. One warp per scheduler runs the epilogue's dependent chain
+// of conversions, divides and stores without any latency hiding; G groups split it G ways.
+constexpr int EPI_GROUPS = Q3_GEMM_EPI_GROUPS;
+constexpr int EPI_THREADS = 128 * EPI_GROUPS;
+constexpr int TC_THREADS = 64 + EPI_THREADS;  // producer warp, MMA warp, epilogue warps
 constexpr int BK = 64;            // K per stage: 64 bf16 = one 128-byte swizzle row
 constexpr int TILE_M = 128;       // MMA M
 constexpr int MAX_STAGES = 12;
@@ -210,6 +218,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0 && lane == 0) {
         // ---------------- producer
         const CUtensorMap *maps[3] = {&tmA0, &tmA1, &tmA2};
+        const uint64_t stream_pol = policy_evict_first();  // weights are read once per step
         // stage layout: [A sub-tiles 0..ksub-1][A1 sub-tiles (gate_up)][X sub-tiles 0..ksub-1]
         auto stage_a = [&](int s, int i, int j) {
             return smem + (size_t)s * a.stage_bytes + (size_t)(i * a.ksub + j) * a.a_tile_bytes;
@@ -229,10 +238,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             for (int j = 0; j < nsub; j++) {
                 const int col = (ks * a.ksub + j) * BK;
                 if (EPI == GATE_UP) {
-                    tma_load_2d(stage_a(s, 0, j), &tmA0, col, row0, &full[s]);
-                    tma_load_2d(stage_a(s, 1, j), &tmA1, col, row0, &full[s]);
+                    tma_load_2d_stream(stage_a(s, 0, j), &tmA0, col, row0, &full[s], stream_pol);
+                    tma_load_2d_stream(stage_a(s, 1, j), &tmA1, col, row0, &full[s], stream_pol);
                 } else {
-                    tma_load_2d(stage_a(s, 0, j), maps[mat], col, row0, &full[s]);
+                    tma_load_2d_stream(stage_a(s, 0, j), maps[mat], col, row0, &full[s], stream_pol);
                 }
             }
         };
@@ -307,7 +316,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---------------- split-K, ranks 1..S-1: push the fp32 partial tile into rank 0's
         // receive buffer (distributed shared memory) and leave; nothing reads this CTA's memory.
         if (warp >= 2 && my_tiles > 0) {
-            const int quarter = warp % 4;
+            const int quarter = warp % 4, group = (warp - 2) / 4;
             const int row_local = quarter * 32 + lane;
             const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
             const int ldr = NA * a.Bp + 4;
@@ -318,7 +327,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             // tcgen05.ld is warp-collective (.sync.aligned): every lane issues it; only the
             // stores are guarded
             const bool store = got && row_local < a.R;
-            for (int c0 = 0; c0 < NA * a.Bp; c0 += 8) {
+            for (int c0 = 8 * group; c0 < NA * a.Bp; c0 += 8 * EPI_GROUPS) {
                 float v[8];
                 tmem_ld8(lane_addr + c0, v);
                 tmem_wait_ld();
@@ -331,11 +340,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             mbar_arrive_remote(recv_full, 0);  // release: the stores above are visible to rank 0
         }
     } else if (warp >= 2) {
-    // ---------------- epilogue (warps 2-5, one accumulator row per thread). With split-K this
+    // ---------------- epilogue (warps 2.., one accumulator row per thread and group). With split-K this
     // is rank 0 of the cluster: its own partial (K steps of rank 0) plus the received partials
     // of ranks 1..S-1, added in rank order.
     pdl_wait();
-    const int quarter = warp % 4;
+    const int quarter = warp % 4, group = (warp - 2) / 4;
     const int row_local = quarter * 32 + lane;
     const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
     const int ldr = NA * a.Bp + 4;
@@ -358,7 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const bool valid = row_local < a.R && m < a.rows[mat];
         bf16 *o = EPI == QKV ? (mat == 0 ? a.out0 : mat == 1 ? a.out1 : a.out2) : a.out0;
         const long long ostride = a.rows[mat];
-        for (int c0 = 0; c0 < a.Bp; c0 += 8) {
+        for (int c0 = 8 * group; c0 < a.Bp; c0 += 8 * EPI_GROUPS) {
             float acc[8], acc2[8];
             tmem_ld8(lane_addr + c0, acc);
             if (EPI == GATE_UP) tmem_ld8(lane_addr + a.Bp + c0, acc2);
