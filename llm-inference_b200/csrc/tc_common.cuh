@@ -40,14 +40,6 @@ __device__ __forceinline__ void tma_load_2d_stream(void *dst, const CUtensorMap 
 #endif
 }
 
-// Brings the box at (x, y) of `map` into L2 without touching shared memory. Safe before the
-// programmatic-dependency wait even for data the previous kernel writes: L2 is the point of
-// coherence, so a later load sees the newer data either way.
-__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *map, int x, int y) {
-    asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(map), "r"(x), "r"(y)
-                 : "memory");
-}
-
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -85,49 +77,6 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-// Loads 8 consecutive 32-bit columns of this thread's TMEM lane. The registers hold their values
-// only once tmem_wait_regs has returned.
-__device__ __forceinline__ void tmem_ld8_u(uint32_t taddr, uint32_t *r) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "r"(taddr)
-                 : "memory");
-}
-
-// tcgen05.wait::ld, with the loaded registers passed through it so that no use of them can be
-// scheduled before the wait.
-template <int N>
-__device__ __forceinline__ void tmem_wait_regs(uint32_t (&r)[N]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < N; i++) asm volatile("" : "+r"(r[i]));
-}
-
-// Tiled bulk store of a shared-memory box to global memory (bulk async-group completion).
-__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, const void *src, int x, int y) {
-    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
-                 "r"(smem_u32(src)), "r"(x), "r"(y)
-                 : "memory");
-}
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-// Waits until every committed bulk store has finished reading shared memory.
-__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
-
-// AND of `v` over the `n` threads of named barrier `id` (every one of them must call it).
-__device__ __forceinline__ bool bar_and(int id, int n, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "barrier.red.and.pred q, %2, %3, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id), "r"(n)
-        : "memory");
-    return r != 0;
-}
-__device__ __forceinline__ void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
 
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float *v) {
     uint32_t r[8];
