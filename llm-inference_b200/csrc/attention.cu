@@ -612,6 +612,15 @@ constexpr int PV_TILE = 128;
 #endif
 constexpr int PV_STAGES = Q3_PV_STAGES;
 constexpr int PV_ACC = 2;
+#ifndef Q3_PV_GROUPS
+#define Q3_PV_GROUPS 2
+#endif
+// p-warp groups: group g computes the probabilities of query heads h with h % PV_GROUPS == g.
+// One warp per scheduler leaves the exp / divide / round chain of every tile without latency
+// hiding; more groups shorten the chain each warp runs per tile.
+constexpr int PV_GROUPS = Q3_PV_GROUPS;
+constexpr int PV_P_THREADS = 128 * PV_GROUPS;
+constexpr int PV_THREADS = 64 + PV_P_THREADS;  // producer warp, MMA warp, p warps
 constexpr int PV_V_BYTES = PV_TILE * 128;      // one 64-dim half of a V tile
 constexpr int PV_P_OFF = 2 * PV_V_BYTES;       // P: 2 swizzle atoms of 16 rows x 128 B
 constexpr int PV_S_OFF = PV_P_OFF + 2 * 16 * 128;
@@ -624,7 +633,7 @@ struct PvTcPlan {
 };
 
 template <int NREP>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(PV_THREADS, 1)
     attn_pv_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a,
                       const __grid_constant__ PvTcPlan pl) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -642,19 +651,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int i = 0; i < PV_STAGES; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&pfull[i], 128);
+            mbar_init(&pfull[i], PV_P_THREADS);
             mbar_init(&empty[i], 1);
         }
         for (int i = 0; i < PV_ACC; i++) {
             mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
+            mbar_init(&acc_empty[i], PV_P_THREADS);
         }
         fence_barrier_init();
         prefetch_tmap(&tmV);
     }
     if (warp >= 2) {  // zero the padding rows NREP..15 of every stage's P once
         const int t = threadIdx.x - 64;
-        for (int j = t; j < PV_STAGES * 2 * 16 * 8; j += 128) {  // 16-byte units
+        for (int j = t; j < PV_STAGES * 2 * 16 * 8; j += PV_P_THREADS) {  // 16-byte units
             const int st = j / 256, r = j % 256, atom = r / 128, row = (r % 128) / 8, c = r % 8;
             if (row >= NREP)
                 *reinterpret_cast<uint4 *>(smem + (size_t)st * PV_STAGE_BYTES + PV_P_OFF + atom * 2048 + row * 128 + c * 16) =
@@ -745,8 +754,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             if (ok) mma_commit(&acc_full[buf]);
         }
     } else if (warp >= 2) {
-        // ---------------- p warps: one position per thread; then the item's epilogue
-        const int t = threadIdx.x - 64;
+        // ---------------- p warps: one position per thread and group; then the item's epilogue
+        const int t = (threadIdx.x - 64) % 128, grp = (threadIdx.x - 64) / 128;
         const int quarter = warp % 4;
         const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
         const int d = quarter * 32 + lane;  // accumulator row = head dim
@@ -768,11 +777,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if (it.nc == 1) {
                     bf16 *o = a.out + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * a.head_dim + d;
 #pragma unroll
-                    for (int h = 0; h < NREP; h++) o[(size_t)h * a.head_dim] = __float2bfloat16(acc[h]);
+                    for (int h = 0; h < NREP; h++)
+                        if (h % PV_GROUPS == grp) o[(size_t)h * a.head_dim] = __float2bfloat16(acc[h]);
                 } else {
                     float *part = a.partial + ((size_t)it.b * a.n_heads + it.kvh * NREP) * a.max_chunks * a.head_dim;
 #pragma unroll
-                    for (int h = 0; h < NREP; h++) part[((size_t)h * a.max_chunks + it.c) * a.head_dim + d] = acc[h];
+                    for (int h = 0; h < NREP; h++)
+                        if (h % PV_GROUPS == grp) part[((size_t)h * a.max_chunks + it.c) * a.head_dim + d] = acc[h];
                 }
             }
             return true;
@@ -805,14 +816,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const int c16 = (t % 64) / 8;
 #pragma unroll
                 for (int h = 0; h < NREP; h++) {
+                    if (h % PV_GROUPS != grp) continue;
                     const float p = t < rows ? round_bf16(expf(s_st[h * PV_TILE + t] - m[h]) / sum[h]) : 0.0f;
                     *reinterpret_cast<bf16 *>(prow + h * 128 + ((c16 ^ (h & 7)) << 4)) = __float2bfloat16(p);
                 }
-                if (t >= rows) {  // V rows past the sequence: zero both halves of row t
-                    uint4 *v0 = reinterpret_cast<uint4 *>(base + t * 128);
-                    uint4 *v1 = reinterpret_cast<uint4 *>(base + PV_V_BYTES + t * 128);
+                if (t >= rows) {  // V rows past the sequence: zero both halves of row t, split over the groups
+                    for (int half = grp; half < 2; half += PV_GROUPS) {
+                        uint4 *v = reinterpret_cast<uint4 *>(base + half * PV_V_BYTES + t * 128);
 #pragma unroll
-                    for (int c = 0; c < 8; c++) v0[c] = v1[c] = make_uint4(0, 0, 0, 0);
+                        for (int c = 0; c < 8; c++) v[c] = make_uint4(0, 0, 0, 0);
+                    }
                 }
                 fence_proxy_async();
                 mbar_arrive(&pfull[st]);
@@ -1033,7 +1046,7 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
     const int grid = (int)std::min<long long>(max_items, num_sms());
-    Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP>, dim3(grid), dim3(TC_THREADS), smem, s, 1, mv, a, pl));
+    Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP>, dim3(grid), dim3(PV_THREADS), smem, s, 1, mv, a, pl));
     return Q3_OK;
 }
 
