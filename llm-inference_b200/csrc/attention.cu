@@ -51,7 +51,6 @@ constexpr int K_STAGES = 2;
 constexpr int VT = 64;           // positions per staged V tile
 constexpr int V_STAGES = 3;
 constexpr int MAX_B = 1024;      // sequences per launch (prefix table in shared memory)
-constexpr int STATS_SMEM = 160 * 1024;  // stats kernel: upper bound of its score staging
 
 struct AttnArgs {
     const bf16 *q;        // sequence b: q + b*q_stride, heads concatenated
@@ -68,7 +67,6 @@ struct AttnArgs {
     int chunk_b;          // positions per pv item
     int sc_chunk;         // positions per scores item
     int max_chunks;       // split mode: capacity of `partial` along the chunk axis
-    int stats_cap;        // stats kernel: floats of shared memory for staged scores
     float scale;
 };
 
@@ -319,20 +317,59 @@ __global__ void __launch_bounds__(SC_THREADS) attn_scores_kernel(const __grid_co
 }
 
 // ------------------------------------------------------------------ stats (split mode)
+// Softmax statistics of every query head of (sequence, kv head) in the reference's order
+// (src/kernels.cu:406-436): for each head, 128 slots, slot s taking positions s, s + 128, ... in
+// order, then an xor tree per warp and the four warp totals in warp order; first the max, then
+// the sum of expf(score - max).
+//
+// One thread per (head, slot): 128 * NREP threads, so that the exp / add chain of each slot is
+// spread over NREP times more warps than one 128-thread block would give it. A thread keeps its
+// first STATS_REG scores in registers between the two passes; longer rows re-read the rest (from
+// L2: the scores kernel wrote them just before).
+constexpr int STATS_REG = 32;
+
 template <int NREP>
-__global__ void __launch_bounds__(THREADS) attn_stats_kernel(const __grid_constant__ AttnArgs a) {
-    extern __shared__ __align__(16) unsigned char smem[];
+__global__ void __launch_bounds__(128 * NREP) attn_stats_kernel(const __grid_constant__ AttnArgs a) {
+    __shared__ float red[NREP][4];
     pdl_trigger();
     pdl_wait();
     const int b = blockIdx.x / a.n_kv, kvh = blockIdx.x % a.n_kv;
     const int len = seq_len(a, b);
     if (len == 0) return;
-    float m[NREP], s[NREP];
-    softmax_stats<NREP>(a, b, kvh, len, reinterpret_cast<float *>(smem), a.stats_cap, m, s);
-    if (threadIdx.x < NREP) {
-        float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + threadIdx.x) * 2;
-        st[0] = m[threadIdx.x];
-        st[1] = s[threadIdx.x];
+    const int h = threadIdx.x / 128, slot = threadIdx.x % 128, lane = slot % 32, w = slot / 32;
+    const float *sc = a.scores + ((size_t)b * a.n_heads + (size_t)kvh * NREP + h) * a.ld;
+    float v[STATS_REG];
+#pragma unroll
+    for (int k = 0; k < STATS_REG; k++) {
+        const int t = slot + 128 * k;
+        v[k] = t < len ? __ldcg(sc + t) : -INFINITY;  // -inf leaves the max unchanged
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < STATS_REG; k++) mx = fmaxf(mx, v[k]);
+    for (int t = slot + 128 * STATS_REG; t < len; t += 128) mx = fmaxf(mx, __ldcg(sc + t));
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[h][w] = mx;
+    __syncthreads();
+    mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; i++) mx = fmaxf(mx, red[h][i]);
+    __syncthreads();  // red is reused for the sums
+    float sm = 0.0f;
+#pragma unroll
+    for (int k = 0; k < STATS_REG; k++)
+        if (slot + 128 * k < len) sm += expf(v[k] - mx);
+    for (int t = slot + 128 * STATS_REG; t < len; t += 128) sm += expf(__ldcg(sc + t) - mx);
+    for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+    if (lane == 0) red[h][w] = sm;
+    __syncthreads();
+    if (slot == 0) {
+        float r = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) r += red[h][i];
+        float *st = a.stats + ((size_t)b * a.n_heads + kvh * NREP + h) * 2;
+        st[0] = mx;
+        st[1] = r;
     }
 }
 
@@ -1019,15 +1056,10 @@ int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
     return Q3_OK;
 }
 
-// Stats kernel with just enough shared memory for every score of its group (several CTAs per
-// SM, one wave), or STATS_SMEM slices for longer caches.
+// One block of 128 * NREP threads per (sequence, kv head).
 template <int NREP>
-int launch_stats(AttnArgs a, cudaStream_t s) {
-    const long long need = (long long)NREP * ((a.max_seq + THREADS - 1) / THREADS * THREADS) * 4;
-    const size_t smem = (size_t)std::min<long long>(need, STATS_SMEM);
-    a.stats_cap = (int)(smem / 4);
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_kernel<NREP>), smem));
-    Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(THREADS), smem, s, 1, a));
+int launch_stats(const AttnArgs &a, cudaStream_t s) {
+    Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(128 * NREP), 0, s, 1, a));
     return Q3_OK;
 }
 
