@@ -49,6 +49,19 @@ int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int 
 int score_ld(int max_seq);
 size_t attention_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, AttnSplit *sp,
                                 float **scores, void *base);
+int gemv_plain_n(bf16 *out, const bf16 *w, const bf16 *x, int rows, int cols, cudaStream_t s, const bf16 *norm_w,
+                 float eps);
+int gemv_qkv_n(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf16 *wv, const bf16 *x, int q_rows,
+               int kv_rows, int cols, cudaStream_t s, const bf16 *norm_w, float eps);
+int gemv_gate_up_n(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int rows, int cols,
+                   bf16 *gate_tap, bf16 *up_tap, cudaStream_t s, const bf16 *norm_w, float eps);
+int fused_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
+size_t fused_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, int chunks,
+                            void *base, float **scores, float **cmax, float **partial, unsigned **ctr);
+int attention_fused(bf16 *out, const bf16 *q, const bf16 *k, const bf16 *v, const bf16 *q_norm_w,
+                    const bf16 *k_norm_w, bf16 *key_cache, bf16 *value_cache, KvLayout kv, const int *pos, int batch,
+                    long long q_stride, long long kv_stride, int n_heads, int n_kv_heads, int head_dim, int max_seq,
+                    float eps, float theta, float scale, int chunks, void *scratch, cudaStream_t s);
 int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s);
 int fill_normal_blocks(bf16 *dst, long long n_blocks, long long block_len, long long block_stride,
                        unsigned long long seed, float mean, float std, cudaStream_t s);
@@ -68,6 +81,9 @@ struct q3_engine {
     void *attn_scratch;
     float *scores;
     AttnSplit split;
+    // small batches: RoPE and attention in one launch (attn_fused.cu), zeroed scratch
+    int fused_chunks = 0;
+    void *fused_scratch = nullptr;
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
     int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
@@ -110,27 +126,53 @@ int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int c
     const float scale = (float)(1.0 / sqrt((double)c.head_dim));
     cudaStream_t s = e->stream;
     const bool exact_attn = (e->flags & Q3_ENGINE_EXACT_ATTENTION) != 0;
+    // rows of a prompt share one cache and read each other's new rows: not in one fused launch
+    const bool fused = e->fused_chunks > 0 && !shared_cache;
+    // one row: the batch-1 projections that read a normed input normalize it themselves
+    const bool norm_in_gemv = rows == 1 && H <= 8192;
+    const float eps = c.rms_norm_eps;
 
     TRY(embedding(e->x, e->embed, tok, rows, H, c.vocab_size, s));
     for (int l = 0; l < c.n_layers; l++) {
         const q3_layer_weights &w = e->layers[l];
         bf16 *kc = e->key_cache + ((size_t)l * B + cache_seq) * seq_stride;
         bf16 *vc = e->value_cache + ((size_t)l * B + cache_seq) * seq_stride;
-        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.attn_norm, rows, H, c.rms_norm_eps, s));
-        TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, rows, qd,
-                     kvd, H, s));
-        TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, pos, rows, qd,
-                         kvd, kv, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, c.rms_norm_eps, c.rope_theta,
-                         nullptr, nullptr, s));
-        TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), pos, rows, qd, kv, c.n_heads,
-                      c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
+        if (norm_in_gemv) {
+            TRY(gemv_qkv_n(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->x, qd, kvd,
+                           H, s, (const bf16 *)w.attn_norm, eps));
+        } else {
+            TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.attn_norm, rows, H, eps, s));
+            TRY(proj_qkv(e->q, e->k, e->v, (const bf16 *)w.wq, (const bf16 *)w.wk, (const bf16 *)w.wv, e->xb, rows,
+                         qd, kvd, H, s));
+        }
+        if (fused) {
+            TRY(attention_fused(e->attn_out, e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc,
+                                kv, pos, rows, qd, kvd, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, eps,
+                                c.rope_theta, scale, e->fused_chunks, e->fused_scratch, s));
+        } else {
+            TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, pos, rows,
+                             qd, kvd, kv, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, eps, c.rope_theta,
+                             nullptr, nullptr, s));
+            TRY(attention(e->attn_out, e->q, kc, vc, e->scores, score_ld(e->max_seq), pos, rows, qd, kv, c.n_heads,
+                          c.n_kv_heads, c.head_dim, e->max_seq, scale, exact_attn ? nullptr : &e->split, s));
+        }
         TRY(proj_residual(e->x, (const bf16 *)w.wo, e->attn_out, rows, H, qd, nullptr, s));
-        TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, rows, H, c.rms_norm_eps, s));
-        TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, rows, I, H, nullptr, nullptr, s));
+        if (norm_in_gemv) {
+            TRY(gemv_gate_up_n(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->x, I, H, nullptr, nullptr, s,
+                               (const bf16 *)w.mlp_norm, eps));
+        } else {
+            TRY(rmsnorm(e->xb, e->x, (const bf16 *)w.mlp_norm, rows, H, eps, s));
+            TRY(proj_gate_up(e->hb, (const bf16 *)w.w_gate, (const bf16 *)w.w_up, e->xb, rows, I, H, nullptr, nullptr,
+                             s));
+        }
         TRY(proj_residual(e->x, (const bf16 *)w.w_down, e->hb, rows, H, I, nullptr, s));
     }
-    TRY(rmsnorm(e->xb, e->x, e->final_norm, rows, H, c.rms_norm_eps, s));
-    TRY(proj(e->logits, e->lm_head, e->xb, rows, c.vocab_size, H, s));
+    if (norm_in_gemv) {
+        TRY(gemv_plain_n(e->logits, e->lm_head, e->x, c.vocab_size, H, s, e->final_norm, eps));
+    } else {
+        TRY(rmsnorm(e->xb, e->x, e->final_norm, rows, H, eps, s));
+        TRY(proj(e->logits, e->lm_head, e->xb, rows, c.vocab_size, H, s));
+    }
     return Q3_OK;
 }
 
@@ -233,6 +275,15 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->step, 16);
     A((void **)&e->pf_token, B * 4);
     A((void **)&e->pf_pos, B * 4);
+    size_t fused_bytes = 0;
+    if (!mk && !(flags & (Q3_ENGINE_EXACT_ATTENTION | Q3_ENGINE_SPLIT_ATTENTION))) {
+        e->fused_chunks = fused_chunks(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq);
+        if (e->fused_chunks > 0) {
+            fused_bytes = fused_scratch_layout(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq, e->fused_chunks,
+                                               nullptr, nullptr, nullptr, nullptr, nullptr);
+            A(&e->fused_scratch, fused_bytes);
+        }
+    }
     if (mk) {
         e->mk = true;
         e->mk_nrep = c.n_heads / c.n_kv_heads;
@@ -254,6 +305,7 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
                              e->attn_scratch);
     cudaStream_t s = e->stream;
     r = record_cuda_error(cudaMemsetAsync(e->attn_scratch, 0, scratch, s));
+    if (r == Q3_OK && e->fused_scratch) r = record_cuda_error(cudaMemsetAsync(e->fused_scratch, 0, fused_bytes, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->key_cache, 0, cache, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->value_cache, 0, cache, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->next_token, 0, B * 4, s));

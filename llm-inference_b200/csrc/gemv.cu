@@ -7,13 +7,23 @@
 // points. Splitting a row into column segments keeps that order because every segment but
 // the last is a multiple of 32 chunks.
 //
-// Memory pipeline (what is new): persistent warps, each owning output rows w, w + W, ... (W =
-// warps of the grid, sized to what is resident). A warp loads up to GV_U 16-byte chunks per lane
+// Memory pipeline (what is new): persistent warps; warp w of CTA b owns output rows
+// w * G + b, w * G + b + W, ... (G CTAs, W = 8 G warps, the grid sized to what is resident on
+// every SM), so consecutive rows go to consecutive CTAs and every SM gets the same number of rows
+// to within one -- a projection of 2560 rows puts 17 or 18 on each of the 148 SMs. A warp loads up to GV_U 16-byte chunks per lane
 // of its row at once (8 KB of one row per warp in flight) with streaming loads that bypass L1
 // and are marked evict-first in L2, then runs the reference's FMA chain over them. The first
 // batch of a warp's first row is loaded before the programmatic-dependency wait, because weights
 // never depend on the previous kernel, and the next row's first batch is loaded before the
 // current row's reduction and store. x is read through L1, where every warp of the SM finds it.
+//
+// Fused RMSNorm (NORM): when the projection's input is rmsnorm(x) (qkv, gate_up and the LM head
+// take the normed residual stream), every CTA recomputes the normed vector itself into shared
+// memory, with the reference rmsnorm_kernel's arithmetic (src/kernels.cu:25-71: 256 threads,
+// thread t summing x[t], x[t + 256], ... with fused multiply-adds, an xor tree per warp, the eight
+// warp sums in order, then bf16(bf16(x * inv_rms) * w)); the norm weight is staged before the
+// programmatic-dependency wait. The separate rmsnorm launch and its dependency hop disappear; the
+// extra reads (x and the weight, a few KB per CTA) come from L2.
 #include <algorithm>
 
 #include "common.cuh"
@@ -38,7 +48,11 @@ struct GemvArgs {
     int rows0, rows1;          // QKV: q_rows, kv_rows
     int units;                 // output rows
     int cols;
+    const bf16 *norm_w;        // NORM: rmsnorm weight [cols]; x is then the raw residual stream
+    float eps;
 };
+
+constexpr int GV_NORM_MAX_COLS = 8192;  // NORM: the normed vector lives in shared memory
 
 template <int EPI>
 __device__ __forceinline__ const bf16 *unit_row(const GemvArgs &a, int u, int r) {
@@ -61,9 +75,11 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
     return v;
 }
 
-template <int EPI, int UR>
+template <int EPI, int UR, bool NORM>
 __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant__ GemvArgs a) {
     constexpr int RPU = EPI == GATE_UP ? 2 : 1;  // weight rows per output unit
+    extern __shared__ __align__(16) bf16 xs[];    // NORM: [cols], the norm weight, then the normed x
+    __shared__ float warp_sums[GV_THREADS / 32];
     const int lane = threadIdx.x % 32;
     const int nw = gridDim.x * (GV_THREADS / 32);
     const int n_vec = a.cols / 8;
@@ -82,11 +98,32 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
         }
     };
 
-    int u = blockIdx.x * (GV_THREADS / 32) + threadIdx.x / 32;
+    int u = (threadIdx.x / 32) * gridDim.x + blockIdx.x;
     pdl_trigger();
     if (u < a.units) load_batch(u, 0);
+    if (NORM)
+        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) xs[i] = a.norm_w[i];
     pdl_wait();
-    const uint4 *xv = reinterpret_cast<const uint4 *>(a.x);
+    if (NORM) {
+        float sum = 0.0f;
+        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) {
+            const float v = __bfloat162float(a.x[i]);
+            sum = __fmaf_rn(v, v, sum);
+        }
+        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+        if (lane == 0) warp_sums[threadIdx.x / 32] = sum;
+        __syncthreads();
+        float total = 0.0f;
+#pragma unroll
+        for (int w_ = 0; w_ < GV_THREADS / 32; w_++) total += warp_sums[w_];
+        const float inv_rms = rsqrtf(total / a.cols + a.eps);
+        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) {  // each thread rewrites its own elements
+            const bf16 normed = __float2bfloat16(__bfloat162float(a.x[i]) * inv_rms);
+            xs[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(xs[i]));
+        }
+        __syncthreads();
+    }
+    const uint4 *xv = reinterpret_cast<const uint4 *>(NORM ? xs : a.x);
     for (; u < a.units; u += nw) {
         float acc[RPU];
 #pragma unroll
@@ -97,7 +134,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
             for (int j = 0; j < UR; j++) {
                 const int i = lane + 32 * (r0 + j);
                 if (i < n_vec) {
-                    const bf16x8 xc = ldg128(xv + i);
+                    const bf16x8 xc = NORM ? lds128(xv + i) : ldg128(xv + i);
 #pragma unroll
                     for (int r = 0; r < RPU; r++) acc[r] = dot8(*reinterpret_cast<const bf16x8 *>(&w[r][j]), xc, acc[r]);
                 }
@@ -136,29 +173,39 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
 
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int EPI, int UR>
+template <int EPI, int UR, bool NORM>
 int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     static int per_sm[64] = {};  // resident CTAs per SM, by device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return Q3_ERR_DEVICE;
+    // NORM: occupancy counted at the largest normed vector, so one grid size fits every width
+    const size_t smem = NORM ? (size_t)a.cols * 2 : 0, smem_plan = NORM ? (size_t)GV_NORM_MAX_COLS * 2 : 0;
     if (per_sm[dev] == 0) {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR>, GV_THREADS, 0) != cudaSuccess || n < 1)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM>, GV_THREADS, smem_plan) !=
+                cudaSuccess ||
+            n < 1)
             n = 1;
         cudaGetLastError();
         per_sm[dev] = n;
     }
-    const long long want = (a.units + GV_THREADS / 32 - 1) / (GV_THREADS / 32);
-    const int grid = (int)std::min<long long>(want, (long long)num_sms() * per_sm[dev]);
-    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR>, dim3(grid), dim3(GV_THREADS), 0, stream, 1, a));
+    // every resident slot (CTA b has rows only if b < units)
+    const int grid = (int)std::min<long long>(a.units, (long long)num_sms() * per_sm[dev]);
+    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM>, dim3(grid), dim3(GV_THREADS), smem, stream, 1, a));
     return Q3_OK;
+}
+
+template <int EPI, int UR>
+int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
+    return a.norm_w ? launch_gemv_ur<EPI, UR, true>(a, stream) : launch_gemv_ur<EPI, UR, false>(a, stream);
 }
 
 template <int EPI>
 int launch_gemv(GemvArgs a, cudaStream_t stream) {
     if (a.units <= 0 || a.cols <= 0) return a.units == 0 ? Q3_OK : Q3_ERR_SHAPE;
     if (a.cols % 8 != 0) return Q3_ERR_SHAPE;
+    if (a.norm_w && (a.cols > GV_NORM_MAX_COLS || (reinterpret_cast<uintptr_t>(a.norm_w) & 15))) return Q3_ERR_SHAPE;
     const int rounds = (a.cols / 8 + 31) / 32;
     if (rounds <= 8) return launch_gemv_ur<EPI, 8>(a, stream);
     if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
@@ -175,10 +222,15 @@ unsigned take_error_gemv() {
     return v;
 }
 
-int gemv_plain(bf16 *out, const bf16 *w, const bf16 *x, int rows, int cols, cudaStream_t s) {
+// The _n variants take an optional rmsnorm: with norm_w, the input is rmsnorm(x, norm_w, eps),
+// computed in the kernel.
+int gemv_plain_n(bf16 *out, const bf16 *w, const bf16 *x, int rows, int cols, cudaStream_t s, const bf16 *norm_w,
+                 float eps) {
     if (!out || !w || !x) return Q3_ERR_ARG;
     if (!aligned16(w) || !aligned16(x)) return Q3_ERR_ALIGN;
     GemvArgs a = {};
+    a.norm_w = norm_w;
+    a.eps = eps;
     a.w0 = w;
     a.x = x;
     a.out0 = out;
@@ -201,12 +253,14 @@ int gemv_residual(bf16 *x, const bf16 *w, const bf16 *in, int rows, int cols, bf
     return launch_gemv<RESIDUAL>(a, s);
 }
 
-int gemv_qkv(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf16 *wv,
-             const bf16 *x, int q_rows, int kv_rows, int cols, cudaStream_t s) {
+int gemv_qkv_n(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf16 *wv,
+               const bf16 *x, int q_rows, int kv_rows, int cols, cudaStream_t s, const bf16 *norm_w, float eps) {
     if (!q || !k || !v || !wq || !wk || !wv || !x) return Q3_ERR_ARG;
     if (!aligned16(wq) || !aligned16(wk) || !aligned16(wv) || !aligned16(x)) return Q3_ERR_ALIGN;
     if (q_rows < 0 || kv_rows < 0) return Q3_ERR_SHAPE;
     GemvArgs a = {};
+    a.norm_w = norm_w;
+    a.eps = eps;
     a.w0 = wq;
     a.w1 = wk;
     a.w2 = wv;
@@ -221,12 +275,14 @@ int gemv_qkv(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf
     return launch_gemv<QKV>(a, s);
 }
 
-int gemv_gate_up(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int rows, int cols,
-                 bf16 *gate_tap, bf16 *up_tap, cudaStream_t s) {
+int gemv_gate_up_n(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int rows, int cols,
+                   bf16 *gate_tap, bf16 *up_tap, cudaStream_t s, const bf16 *norm_w, float eps) {
     if (!act || !w_gate || !w_up || !x) return Q3_ERR_ARG;
     if ((gate_tap == nullptr) != (up_tap == nullptr)) return Q3_ERR_ARG;
     if (!aligned16(w_gate) || !aligned16(w_up) || !aligned16(x)) return Q3_ERR_ALIGN;
     GemvArgs a = {};
+    a.norm_w = norm_w;
+    a.eps = eps;
     a.w0 = w_gate;
     a.w1 = w_up;
     a.x = x;
@@ -236,6 +292,20 @@ int gemv_gate_up(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x,
     a.units = rows;
     a.cols = cols;
     return launch_gemv<GATE_UP>(a, s);
+}
+
+int gemv_plain(bf16 *out, const bf16 *w, const bf16 *x, int rows, int cols, cudaStream_t s) {
+    return gemv_plain_n(out, w, x, rows, cols, s, nullptr, 0.0f);
+}
+
+int gemv_qkv(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const bf16 *wv, const bf16 *x, int q_rows,
+             int kv_rows, int cols, cudaStream_t s) {
+    return gemv_qkv_n(q, k, v, wq, wk, wv, x, q_rows, kv_rows, cols, s, nullptr, 0.0f);
+}
+
+int gemv_gate_up(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int rows, int cols,
+                 bf16 *gate_tap, bf16 *up_tap, cudaStream_t s) {
+    return gemv_gate_up_n(act, w_gate, w_up, x, rows, cols, gate_tap, up_tap, s, nullptr, 0.0f);
 }
 
 }  // namespace q3

@@ -135,7 +135,8 @@ class Engine:
     """Batched greedy decode of `batch` independent sequences (csrc/engine.cu)."""
 
     def __init__(self, weights: DeviceWeights, batch: int, max_seq: int, history_cap: int = 0,
-                 exact_attention: bool = False, stream=None, megakernel: bool = False):
+                 exact_attention: bool = False, stream=None, megakernel: bool = False,
+                 split_attention: bool = False):
         import torch
         load()
         self.weights = weights
@@ -150,7 +151,8 @@ class Engine:
         self.stream = stream
         handle = ctypes.c_void_p()
         call("q3_engine_create", ctypes.byref(self.cfg), ctypes.byref(self._w), batch, max_seq, history_cap,
-             (1 if exact_attention else 0) | (2 if megakernel else 0), self.stream, ctypes.byref(handle))
+             (1 if exact_attention else 0) | (2 if megakernel else 0) | (4 if split_attention else 0), self.stream,
+             ctypes.byref(handle))
         self.handle = handle
         info = Q3EngineBuffers()
         call("q3_engine_info", self.handle, ctypes.byref(info))
