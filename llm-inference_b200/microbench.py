@@ -19,7 +19,8 @@ kernel's algorithmic bytes (every byte it must move once) ÷ that time against t
 copy peak in MEASURED_PEAKS.json.
 
     python llm-inference_b200/microbench.py [--model qwen3-1.7b] [--batch 1 16 64 256]
-        [--kernels rmsnorm qk_norm_rope gate_up o_proj down embedding qkv lm_head attention argmax]
+        [--kernels rmsnorm qk_norm_rope gate_up o_proj down embedding qkv lm_head attention
+                   rope_attention argmax]
         [--kv 4096] [--iters 20] [--warmup 3]
 
 One JSON line per (kernel, batch).
@@ -37,7 +38,7 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent
 
 DEFAULT_KERNELS = ["rmsnorm", "qk_norm_rope", "gate_up", "o_proj", "down", "embedding"]
-ALL_KERNELS = DEFAULT_KERNELS + ["qkv", "lm_head", "attention", "argmax"]
+ALL_KERNELS = DEFAULT_KERNELS + ["qkv", "lm_head", "attention", "rope_attention", "argmax"]
 
 
 def _package():
@@ -222,6 +223,33 @@ class Bench:
                                     *strides, scratch.data_ptr(), pos.data_ptr(), B, nq, nkv, hd, max_seq, scale, s)
         return f, B * L * nkv * hd * 2 * 2 + 2 * B * nq * hd * 2
 
+    def k_rope_attention(self, B):
+        """RoPE + attention in one launch (q3_rope_attention_batched, the engine's path for small
+        batches) over head-major caches; every sequence at position --kv - 1. None when the fused
+        kernel does not apply to the batch."""
+        t, s_ = self.torch, self.s
+        nq, nkv, hd, L = s_.num_attention_heads, s_.num_key_value_heads, s_.head_dim, self.args.kv
+        max_seq = L
+        chunks = self.lib.load().q3_rope_attention_chunks(B, nq, nkv, hd, max_seq)
+        if chunks <= 0:
+            return None
+        kc = self.rn(B, nkv, max_seq, hd)
+        vc = self.rn(B, nkv, max_seq, hd)
+        q, k, v = self.rn(B, nq * hd), self.rn(B, nkv * hd), self.rn(B, nkv * hd)
+        qn, kn = self.rn(hd, std=0.02, mean=1.0), self.rn(hd, std=0.02, mean=1.0)
+        out = t.empty_like(q)
+        pos = t.full((B,), L - 1, dtype=t.int32, device="cuda")
+        nbytes = self.lib.load().q3_rope_attention_scratch_bytes(B, nq, nkv, hd, max_seq, chunks)
+        scratch = t.zeros(nbytes, dtype=t.uint8, device="cuda")
+        strides = (nkv * max_seq * hd, hd, max_seq * hd)
+        scale = 1.0 / math.sqrt(hd)
+        f = lambda s: self.lib.call("q3_rope_attention_batched", out.data_ptr(), q.data_ptr(), k.data_ptr(),
+                                    v.data_ptr(), qn.data_ptr(), kn.data_ptr(), kc.data_ptr(), vc.data_ptr(), *strides,
+                                    pos.data_ptr(), B, nq, nkv, hd, max_seq, 1e-6, s_.rope_theta, scale, chunks,
+                                    scratch.data_ptr(), s)
+        # K and V rows of positions 0..L-2 read, q/k/v read, the output and two cache rows written
+        return f, B * (L - 1) * nkv * hd * 2 * 2 + B * (2 * nq + 4 * nkv) * hd * 2
+
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -240,7 +268,12 @@ def main(argv=None):
     q3 = sys.modules["llm_inference_b200"]
     for name in args.kernels:
         for B in args.batch:
-            launch, nbytes = getattr(b, "k_" + name)(B)
+            made = getattr(b, "k_" + name)(B)
+            if made is None:
+                print(json.dumps({"kernel": name, "model": args.model, "batch": B, "skipped": "not applicable"}),
+                      flush=True)
+                continue
+            launch, nbytes = made
             us = b.time(launch)
             gbs = nbytes / (us * 1e-6) / 1e9
             if q3.device_error() != 0:
