@@ -194,27 +194,26 @@ int q3_attention_batched_static(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *k
  * in one launch: q, k and v are the raw projections (unchanged by the call; the roped rows are
  * not written back), the new key and value rows go to row d_pos[b] of the caches (strides as
  * above), and out receives the attention output. Each (sequence, kv head)'s positions are cut
- * into `chunks` contiguous ranges, one CTA each, which meet once at a barrier in device memory;
- * probabilities are the reference's bit for bit, and only the fp32 order of the P.V sum differs
- * (chunk partials added in chunk order; chunks = 1 gives the reference's output bit for bit).
+ * into `chunks` contiguous ranges, the CTAs of one thread-block cluster, which exchange the
+ * softmax statistics and their partial outputs through distributed shared memory; it needs no
+ * scratch memory. Probabilities are the reference's bit for bit, and only the fp32 order of the
+ * P.V sum differs (chunk partials added in chunk order; chunks = 1 gives the reference's output
+ * bit for bit).
  *   - q3_rope_attention_chunks gives the chunk count for `batch` sequences of up to max_seq
- *     positions on the current device (it fills the GPU), or 0 when the kernel does not apply:
- *     head_dim other than 64 or 128, n_heads / n_kv_heads other than 1, 2, 4 or 8, too many
- *     sequences for one wave, or a chunk whose scores do not fit in shared memory.
- *   - `scratch` holds q3_rope_attention_scratch_bytes(...) bytes and must be zero-filled before
- *     its first use; every call leaves it ready for the next. Calls sharing a scratch buffer must
- *     not overlap on the GPU.
- *   - batch * n_kv_heads * chunks CTAs must fit on the GPU at once (Q3_ERR_SHAPE otherwise), and
- *     with batch > 1 the sequences must have separate caches (cache_seq_stride > 0).
+ *     positions on the current device (16, 8, 4 or 2: the largest whose clusters all fit at
+ *     once), or 0 when the kernel does not apply: head_dim other than 64 or 128,
+ *     n_heads / n_kv_heads other than 1, 2, 4 or 8, or too many sequences.
+ *   - chunks is 1 to 16; Q3_ERR_SHAPE if one cluster of that size (with its chunk's scores in
+ *     shared memory) does not fit on the device. With batch > 1 the sequences must have separate
+ *     caches (cache_seq_stride > 0).
  * No counterpart in the reference (it launches the two kernels one after the other). */
 int q3_rope_attention_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
-size_t q3_rope_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, int chunks);
 int q3_rope_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *k, const q3_bf16 *v,
                               const q3_bf16 *q_norm_w, const q3_bf16 *k_norm_w, q3_bf16 *key_cache,
                               q3_bf16 *value_cache, long long cache_seq_stride, long long cache_pos_stride,
                               long long cache_head_stride, const int *d_pos, int batch, int n_heads, int n_kv_heads,
                               int head_dim, int max_seq, float eps, float theta, float scale, int chunks,
-                              void *scratch, void *stream);
+                              void *stream);
 
 /* out[b] = argmax of x[b][0..n) with argmax_forward's tie and NaN rules. */
 int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream);

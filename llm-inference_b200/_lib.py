@@ -49,9 +49,8 @@ SIGNATURES: dict[str, list] = {
     "q3_attention_batched": [_P, _P, _P, _P, _LL, _LL, _LL, _P, _P, _I, _I, _I, _I, _I, _F, _P],
     "q3_attention_batched_static": [_P, _P, _P, _P, _LL, _LL, _LL, _P, _I, _I, _I, _I, _I, _F, _P],
     "q3_rope_attention_chunks": [_I, _I, _I, _I, _I],
-    "q3_rope_attention_scratch_bytes": [_I, _I, _I, _I, _I, _I],
     "q3_rope_attention_batched": [_P, _P, _P, _P, _P, _P, _P, _P, _LL, _LL, _LL, _P, _I, _I, _I, _I, _I, _F, _F, _F,
-                                  _I, _P, _P],
+                                  _I, _P],
     "q3_argmax_batched": [_P, _P, _I, _I, _P],
     "q3_fill_normal_bf16": [_P, _LL, ctypes.c_ulonglong, _F, _F, _P],
     "q3_weight_bytes_per_step": [_P],
@@ -68,7 +67,6 @@ SIGNATURES: dict[str, list] = {
     "q3_engine_info": [_P, _P],
 }
 RESTYPES = {"q3_status_string": ctypes.c_char_p, "q3_attention_scratch_bytes": ctypes.c_size_t,
-            "q3_rope_attention_scratch_bytes": ctypes.c_size_t,
             "q3_weight_bytes_per_step": ctypes.c_size_t, "q3_kv_bytes_per_position": ctypes.c_size_t}
 
 _lib = None

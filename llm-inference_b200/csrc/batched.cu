@@ -37,12 +37,10 @@ int attention(bf16 *out, const bf16 *q, const bf16 *key_cache, const bf16 *value
               int head_dim, int max_seq, float scale, const AttnSplit *split, cudaStream_t s);
 int attention_check(int n_heads, int n_kv_heads, int head_dim, int max_seq, int n_rows);
 int fused_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
-size_t fused_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, int chunks,
-                            void *base, float **scores, float **cmax, float **partial, unsigned **ctr);
 int attention_fused(bf16 *out, const bf16 *q, const bf16 *k, const bf16 *v, const bf16 *q_norm_w,
                     const bf16 *k_norm_w, bf16 *key_cache, bf16 *value_cache, KvLayout kv, const int *pos, int batch,
                     long long q_stride, long long kv_stride, int n_heads, int n_kv_heads, int head_dim, int max_seq,
-                    float eps, float theta, float scale, int chunks, void *scratch, cudaStream_t s);
+                    float eps, float theta, float scale, int chunks, cudaStream_t s);
 
 // ---------------------------------------------------------------- batched projections
 
@@ -220,25 +218,17 @@ int q3_rope_attention_chunks(int batch, int n_heads, int n_kv_heads, int head_di
     return fused_chunks(batch, n_heads, n_kv_heads, head_dim, max_seq);
 }
 
-size_t q3_rope_attention_scratch_bytes(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, int chunks) {
-    if (batch <= 0 || n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads != 0 || head_dim <= 0 ||
-        max_seq <= 0 || chunks <= 0)
-        return 0;
-    return fused_scratch_layout(batch, n_heads, n_kv_heads, head_dim, max_seq, chunks, nullptr, nullptr, nullptr,
-                                nullptr, nullptr);
-}
-
 int q3_rope_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *k, const q3_bf16 *v,
                               const q3_bf16 *q_norm_w, const q3_bf16 *k_norm_w, q3_bf16 *key_cache,
                               q3_bf16 *value_cache, long long cache_seq_stride, long long cache_pos_stride,
                               long long cache_head_stride, const int *d_pos, int batch, int n_heads, int n_kv_heads,
                               int head_dim, int max_seq, float eps, float theta, float scale, int chunks,
-                              void *scratch, void *stream) {
+                              void *stream) {
     DEVICE_OR_RETURN();
     const KvLayout kv = {cache_seq_stride, cache_pos_stride, cache_head_stride};
     return attention_fused(B(out), CB(q), CB(k), CB(v), CB(q_norm_w), CB(k_norm_w), B(key_cache), B(value_cache), kv,
                            d_pos, batch, (long long)n_heads * head_dim, (long long)n_kv_heads * head_dim, n_heads,
-                           n_kv_heads, head_dim, max_seq, eps, theta, scale, chunks, scratch, S(stream));
+                           n_kv_heads, head_dim, max_seq, eps, theta, scale, chunks, S(stream));
 }
 
 int q3_argmax_batched(int *out, const q3_bf16 *x, int batch, int n, void *stream) {

@@ -56,12 +56,10 @@ int gemv_qkv_n(bf16 *q, bf16 *k, bf16 *v, const bf16 *wq, const bf16 *wk, const 
 int gemv_gate_up_n(bf16 *act, const bf16 *w_gate, const bf16 *w_up, const bf16 *x, int rows, int cols,
                    bf16 *gate_tap, bf16 *up_tap, cudaStream_t s, const bf16 *norm_w, float eps);
 int fused_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq);
-size_t fused_scratch_layout(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq, int chunks,
-                            void *base, float **scores, float **cmax, float **partial, unsigned **ctr);
 int attention_fused(bf16 *out, const bf16 *q, const bf16 *k, const bf16 *v, const bf16 *q_norm_w,
                     const bf16 *k_norm_w, bf16 *key_cache, bf16 *value_cache, KvLayout kv, const int *pos, int batch,
                     long long q_stride, long long kv_stride, int n_heads, int n_kv_heads, int head_dim, int max_seq,
-                    float eps, float theta, float scale, int chunks, void *scratch, cudaStream_t s);
+                    float eps, float theta, float scale, int chunks, cudaStream_t s);
 int fill_normal(bf16 *dst, long long n, unsigned long long seed, float mean, float std, cudaStream_t s);
 int fill_normal_blocks(bf16 *dst, long long n_blocks, long long block_len, long long block_stride,
                        unsigned long long seed, float mean, float std, cudaStream_t s);
@@ -81,9 +79,8 @@ struct q3_engine {
     void *attn_scratch;
     float *scores;
     AttnSplit split;
-    // small batches: RoPE and attention in one launch (attn_fused.cu), zeroed scratch
+    // small batches: RoPE and attention in one launch (attn_fused.cu), this many chunks per head
     int fused_chunks = 0;
-    void *fused_scratch = nullptr;
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
     int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
@@ -148,7 +145,7 @@ int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int c
         if (fused) {
             TRY(attention_fused(e->attn_out, e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc,
                                 kv, pos, rows, qd, kvd, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, eps,
-                                c.rope_theta, scale, e->fused_chunks, e->fused_scratch, s));
+                                c.rope_theta, scale, e->fused_chunks, s));
         } else {
             TRY(qk_norm_rope(e->q, e->k, e->v, (const bf16 *)w.q_norm, (const bf16 *)w.k_norm, kc, vc, pos, rows,
                              qd, kvd, kv, c.n_heads, c.n_kv_heads, c.head_dim, e->max_seq, eps, c.rope_theta,
@@ -275,15 +272,8 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->step, 16);
     A((void **)&e->pf_token, B * 4);
     A((void **)&e->pf_pos, B * 4);
-    size_t fused_bytes = 0;
-    if (!mk && !(flags & (Q3_ENGINE_EXACT_ATTENTION | Q3_ENGINE_SPLIT_ATTENTION))) {
+    if (!mk && !(flags & (Q3_ENGINE_EXACT_ATTENTION | Q3_ENGINE_SPLIT_ATTENTION)))
         e->fused_chunks = fused_chunks(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq);
-        if (e->fused_chunks > 0) {
-            fused_bytes = fused_scratch_layout(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq, e->fused_chunks,
-                                               nullptr, nullptr, nullptr, nullptr, nullptr);
-            A(&e->fused_scratch, fused_bytes);
-        }
-    }
     if (mk) {
         e->mk = true;
         e->mk_nrep = c.n_heads / c.n_kv_heads;
@@ -305,7 +295,6 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
                              e->attn_scratch);
     cudaStream_t s = e->stream;
     r = record_cuda_error(cudaMemsetAsync(e->attn_scratch, 0, scratch, s));
-    if (r == Q3_OK && e->fused_scratch) r = record_cuda_error(cudaMemsetAsync(e->fused_scratch, 0, fused_bytes, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->key_cache, 0, cache, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->value_cache, 0, cache, s));
     if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->next_token, 0, B * 4, s));

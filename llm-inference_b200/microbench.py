@@ -239,14 +239,11 @@ class Bench:
         qn, kn = self.rn(hd, std=0.02, mean=1.0), self.rn(hd, std=0.02, mean=1.0)
         out = t.empty_like(q)
         pos = t.full((B,), L - 1, dtype=t.int32, device="cuda")
-        nbytes = self.lib.load().q3_rope_attention_scratch_bytes(B, nq, nkv, hd, max_seq, chunks)
-        scratch = t.zeros(nbytes, dtype=t.uint8, device="cuda")
         strides = (nkv * max_seq * hd, hd, max_seq * hd)
         scale = 1.0 / math.sqrt(hd)
         f = lambda s: self.lib.call("q3_rope_attention_batched", out.data_ptr(), q.data_ptr(), k.data_ptr(),
                                     v.data_ptr(), qn.data_ptr(), kn.data_ptr(), kc.data_ptr(), vc.data_ptr(), *strides,
-                                    pos.data_ptr(), B, nq, nkv, hd, max_seq, 1e-6, s_.rope_theta, scale, chunks,
-                                    scratch.data_ptr(), s)
+                                    pos.data_ptr(), B, nq, nkv, hd, max_seq, 1e-6, s_.rope_theta, scale, chunks, s)
         # K and V rows of positions 0..L-2 read, q/k/v read, the output and two cache rows written
         return f, B * (L - 1) * nkv * hd * 2 * 2 + B * (2 * nq + 4 * nkv) * hd * 2
 

@@ -8,8 +8,7 @@ by the drop-in attention_forward (bit-identical to the reference's attention) pe
   - with the chunk count that fills the GPU, only the fp32 order of the P.V sum differs: the
     split-attention tolerance of test_batched_gpu.py applies (at most 1 bf16 ulp for all but
     0.5 % of elements, every element within 2^-7 |ref| + 2^-17 sum |p v|);
-  - every case runs twice on the same scratch (its counters must come back to zero), and cache
-    rows past each position hold NaN, which must never be read.
+  - every case runs twice, and cache rows past each position hold NaN, which must never be read.
 """
 import math
 import sys
@@ -81,15 +80,13 @@ def test_rope_attention_matches_exact_kernels(batch, n_heads, n_kv, hd, position
     ref_kc, ref_vc, ref_out = reference(q, k, v, qn, kn, kc, vc, pos, n_heads, n_kv, hd, max_seq, scale)
     strides = cache_strides(layout, max_seq, n_kv, hd)
     q0, k0, v0 = q.clone(), k.clone(), v.clone()
-    for chunks in (1, auto):
-        nbytes = lib.q3_rope_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq, chunks)
-        scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    for chunks in sorted({1, 3, auto}):
         for rep in range(2):
             kl, vl = to_layout(kc, layout, n_kv, hd), to_layout(vc, layout, n_kv, hd)
             out = torch.full_like(q, float("nan"))
             _lib.call("q3_rope_attention_batched", out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                       qn.data_ptr(), kn.data_ptr(), kl.data_ptr(), vl.data_ptr(), *strides, pos.data_ptr(), batch,
-                      n_heads, n_kv, hd, max_seq, EPS, THETA, scale, chunks, scratch.data_ptr(), stream())
+                      n_heads, n_kv, hd, max_seq, EPS, THETA, scale, chunks, stream())
             torch.cuda.synchronize()
             assert q3.device_error() == 0
             assert torch.equal(q, q0) and torch.equal(k, k0) and torch.equal(v, v0)
@@ -110,20 +107,17 @@ def test_rope_attention_rejects_bad_arguments():
     assert auto >= 2
     assert lib.q3_rope_attention_chunks(batch, n_heads, n_kv, 96, max_seq) == 0  # head_dim 96: not this kernel
     assert lib.q3_rope_attention_chunks(batch, 24, 8, 128, max_seq) == 0           # group size 3
-    assert lib.q3_rope_attention_chunks(4096, n_heads, n_kv, hd, max_seq) == 0     # more than one wave
+    assert lib.q3_rope_attention_chunks(4096, n_heads, n_kv, hd, max_seq) == 0     # too many sequences
     assert lib.q3_rope_attention_chunks(1, n_heads, n_kv, hd, 10 ** 7) == 0        # chunk scores too long
     t = torch.zeros(batch * max_seq * n_kv * hd, dtype=torch.bfloat16, device="cuda")
     pos = torch.zeros(batch, dtype=torch.int32, device="cuda")
-    scratch = torch.zeros(lib.q3_rope_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq, auto),
-                          dtype=torch.uint8, device="cuda")
     strides = cache_strides("head", max_seq, n_kv, hd)
     args = [t.data_ptr()] * 8 + list(strides) + [pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, EPS, THETA, 0.1]
-    with pytest.raises(q3.Q3Error):  # more chunks than the kernel takes
-        _lib.call("q3_rope_attention_batched", *args, 10 ** 6, scratch.data_ptr(), stream())
+    with pytest.raises(q3.Q3Error):  # more chunks than a cluster takes
+        _lib.call("q3_rope_attention_batched", *args, 17, stream())
     with pytest.raises(q3.Q3Error):  # sequences sharing one cache
-        _lib.call("q3_rope_attention_batched", *args[:8], 0, *strides[1:], *args[11:], auto, scratch.data_ptr(),
-                  stream())
-    with pytest.raises(q3.Q3Error):  # no scratch
-        _lib.call("q3_rope_attention_batched", *args, auto, None, stream())
+        _lib.call("q3_rope_attention_batched", *args[:8], 0, *strides[1:], *args[11:], auto, stream())
+    with pytest.raises(q3.Q3Error):  # no output
+        _lib.call("q3_rope_attention_batched", None, *args[1:], auto, stream())
     torch.cuda.synchronize()
     assert q3.device_error() == 0
