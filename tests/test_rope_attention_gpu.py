@@ -80,7 +80,16 @@ def test_rope_attention_matches_exact_kernels(batch, n_heads, n_kv, hd, position
     ref_kc, ref_vc, ref_out = reference(q, k, v, qn, kn, kc, vc, pos, n_heads, n_kv, hd, max_seq, scale)
     strides = cache_strides(layout, max_seq, n_kv, hd)
     q0, k0, v0 = q.clone(), k.clone(), v.clone()
-    for chunks in sorted({1, 3, auto}):
+    # one chunk holds every position's scores in shared memory: too many at 8 query heads per kv
+    # head and 2600 positions, which the call refuses
+    one = [1] if n_heads // n_kv <= 4 else []
+    if not one:
+        with pytest.raises(q3.Q3Error) as err:
+            _lib.call("q3_rope_attention_batched", q.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr(),
+                      kn.data_ptr(), kc.data_ptr(), vc.data_ptr(), *cache_strides("ref", max_seq, n_kv, hd),
+                      pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, EPS, THETA, scale, 1, stream())
+        assert err.value.status == 1  # Q3_ERR_SHAPE, and nothing launched
+    for chunks in sorted(set(one + [3, auto])):
         for rep in range(2):
             kl, vl = to_layout(kc, layout, n_kv, hd), to_layout(vc, layout, n_kv, hd)
             out = torch.full_like(q, float("nan"))
