@@ -22,9 +22,11 @@
 //      shared memory (exact: max does not depend on order), and replaces its scores by
 //      e = expf(s - max);
 //   5. (cluster barrier) sums e over all positions in the reference's order -- 128 slots, slot j
-//      taking positions j, j + 128, ... serially (each position's e read from the CTA that holds
-//      it), an xor tree per warp, the four warp totals in order -- so that
-//      p = round_bf16(e / sum) is the reference's probability bit for bit;
+//      taking positions j, j + 128, ... serially, an xor tree per warp, the four warp totals in
+//      order -- so that p = round_bf16(e / sum) is the reference's probability bit for bit. The
+//      NREP * 128 (head, slot) chains are shared out over the cluster's CTAs, one thread each,
+//      reading each position's e from the CTA that holds it; (cluster barrier) every CTA then
+//      gathers the chain sums and finishes the tree itself;
 //   6. accumulates p * v over its chunk in position order (one fused multiply-add chain per
 //      output element) into its shared memory;
 //   7. (cluster barrier) adds the C chunk partials of its slice of the outputs in chunk order and
@@ -100,6 +102,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     __shared__ float wred[NREP][FA_TILE / 32];
     __shared__ float cm_s[FA_MAX_CLUSTER * NREP];
     __shared__ float gmax_s[NREP], gsum_s[NREP];
+    __shared__ float chs[NREP * FA_TILE];  // sums of the chains this CTA computes (per_cta <= NREP * 128)
 
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid % 32;
@@ -305,37 +308,50 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         ex[h * a.cap + i] = expf(ex[h * a.cap + i] - gmax_s[h]);
     }
 
-    // ---- 5. the sum of e in the reference's order (src/kernels.cu:469-470, block_sum :406-420):
-    // slot j adds positions j, j + 128, ... serially, each read from the CTA holding it (SB per
-    // head and thread in flight at once); then the xor tree and the warp totals in order
+    // ---- 5. the sum of e in the reference's order (src/kernels.cu:469-470, block_sum :406-420).
+    // Each (head, slot) chain -- slot j adding positions j, j + 128, ... serially -- is computed by
+    // one thread of one CTA of the cluster (chain i by CTA i / per_cta), which reads each position's
+    // e from the CTA holding it, SB values in flight at once; after a cluster barrier every CTA
+    // gathers the 128 chain sums of each head and runs the xor tree and the warp totals in order.
     cluster.sync();
     {
-        const int slot = tid % FA_TILE;  // FA_TILE == 128 slots
-        constexpr int SB = HPT <= 2 ? 16 : 8;
-        float sm[HPT];
+        constexpr int SB = 16;
+        const int n_chains = NREP * FA_TILE;
+        const int per_cta = (n_chains + C - 1) / C;
+        for (int i = tid; i < per_cta; i += FA_THREADS) {  // more chains than threads below 2 chunks
+            const int chain = c * per_cta + i;
+            float sum = 0.0f;
+            if (chain < n_chains) {
+                const int h = chain / FA_TILE, slot = chain % FA_TILE;
+                int owner = slot / CH, off = slot - owner * CH;  // position slot + 128 m, tracked by holder
+                for (int t = slot; t < len; t += SB * FA_TILE) {
+                    float vals[SB];
 #pragma unroll
-        for (int k = 0; k < HPT; k++) sm[k] = 0.0f;
-        for (int t = slot; t < len; t += SB * 128) {
-            float v[HPT][SB];
+                    for (int j = 0; j < SB; j++) {
+                        vals[j] = t + j * FA_TILE < len ? cluster.map_shared_rank(ex, owner)[h * a.cap + off] : 0.0f;
+                        off += FA_TILE;
+                        while (off >= CH) {
+                            off -= CH;
+                            owner++;
+                        }
+                    }
 #pragma unroll
-            for (int j = 0; j < SB; j++) {
-                const int tt = t + j * 128;
-                const int owner = tt / CH;
-                const float *src = tt < len ? cluster.map_shared_rank(ex, owner) + (tt - owner * CH) : nullptr;
-#pragma unroll
-                for (int k = 0; k < HPT; k++)
-                    v[k][j] = (hgp + HG * k < NREP && tt < len) ? src[(hgp + HG * k) * a.cap] : 0.0f;
+                    for (int j = 0; j < SB; j++)
+                        if (t + j * FA_TILE < len) sum += vals[j];
+                }
             }
-#pragma unroll
-            for (int k = 0; k < HPT; k++)
-#pragma unroll
-                for (int j = 0; j < SB; j++)
-                    if (hgp + HG * k < NREP && t + j * 128 < len) sm[k] += v[k][j];
+            chs[i] = sum;
         }
+    }
+    cluster.sync();
+    {
+        const int slot = tid % FA_TILE;
+        const int per_cta = (NREP * FA_TILE + C - 1) / C;
 #pragma unroll
         for (int k = 0; k < HPT; k++) {
             const int h = hgp + HG * k;
-            float x = sm[k];
+            const int chain = (h < NREP ? h : 0) * FA_TILE + slot;
+            float x = h < NREP ? *cluster.map_shared_rank(chs + chain % per_cta, chain / per_cta) : 0.0f;
             for (int off = 16; off > 0; off >>= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
             if (h < NREP && lane == 0) wred[h][slot / 32] = x;
         }
@@ -347,7 +363,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
             gsum_s[tid] = x;
         }
         __syncthreads();
-        // probabilities of this chunk (src/kernels.cu:472-474); the e values stay for the others
+        // probabilities of this chunk (src/kernels.cu:472-474)
         for (int e = tid; e < NREP * n_own; e += FA_THREADS) {
             const int h = e / n_own, i = e - h * n_own;
             pr[h * a.cap + i] = round_bf16(ex[h * a.cap + i] / gsum_s[h]);
