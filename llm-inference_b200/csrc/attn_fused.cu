@@ -315,32 +315,44 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     // gathers the 128 chain sums of each head and runs the xor tree and the warp totals in order.
     cluster.sync();
     {
-        constexpr int SB = 16;
+        // tpc lanes of one warp share a chain: lane q loads its elements m = q, q + tpc, ...
+        // (position slot + 128 m), all of a batch in flight at once, and the chain is folded in
+        // order m = 0, 1, 2, ... through shuffles
+        constexpr int SB = 8;
         const int n_chains = NREP * FA_TILE;
         const int per_cta = (n_chains + C - 1) / C;
-        for (int i = tid; i < per_cta; i += FA_THREADS) {  // more chains than threads below 2 chunks
+        int tpc = 1;
+        while (tpc < 32 && 2 * tpc * per_cta <= FA_THREADS) tpc *= 2;
+        const int cpi = FA_THREADS / tpc;           // chains per pass of the block
+        const int m_max = (len + FA_TILE - 1) / FA_TILE;  // elements of the longest chain (slot 0)
+        const int q = lane % tpc, lane0 = lane - q;
+        for (int i0 = 0; i0 < per_cta; i0 += cpi) {
+            const int i = i0 + tid / tpc;
             const int chain = c * per_cta + i;
+            const bool valid = i < per_cta && chain < n_chains;
+            const int h = valid ? chain / FA_TILE : 0, slot = valid ? chain % FA_TILE : 0;
+            const int m_end = valid && slot < len ? (len - 1 - slot) / FA_TILE + 1 : 0;  // this chain's elements
             float sum = 0.0f;
-            if (chain < n_chains) {
-                const int h = chain / FA_TILE, slot = chain % FA_TILE;
-                int owner = slot / CH, off = slot - owner * CH;  // position slot + 128 m, tracked by holder
-                for (int t = slot; t < len; t += SB * FA_TILE) {
-                    float vals[SB];
+            for (int mb = 0; mb < m_max; mb += SB * tpc) {  // uniform over the block
+                float vals[SB];
 #pragma unroll
-                    for (int j = 0; j < SB; j++) {
-                        vals[j] = t + j * FA_TILE < len ? cluster.map_shared_rank(ex, owner)[h * a.cap + off] : 0.0f;
-                        off += FA_TILE;
-                        while (off >= CH) {
-                            off -= CH;
-                            owner++;
-                        }
+                for (int j = 0; j < SB; j++) {
+                    const int m = mb + j * tpc + q;
+                    float x = 0.0f;
+                    if (m < m_end) {
+                        const int t = slot + m * FA_TILE, owner = t / CH;
+                        x = cluster.map_shared_rank(ex, owner)[h * a.cap + (t - owner * CH)];
                     }
-#pragma unroll
-                    for (int j = 0; j < SB; j++)
-                        if (t + j * FA_TILE < len) sum += vals[j];
+                    vals[j] = x;
                 }
+#pragma unroll
+                for (int j = 0; j < SB; j++)
+                    for (int r = 0; r < tpc; r++) {
+                        const float x = __shfl_sync(0xffffffffu, vals[j], lane0 + r);
+                        if (mb + j * tpc + r < m_end) sum += x;
+                    }
             }
-            chs[i] = sum;
+            if (valid && q == 0) chs[i] = sum;
         }
     }
     cluster.sync();
