@@ -200,8 +200,8 @@ int q3_attention_batched_static(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *k
  * P.V sum differs (chunk partials added in chunk order; chunks = 1 gives the reference's output
  * bit for bit).
  *   - q3_rope_attention_chunks gives the chunk count for `batch` sequences of up to max_seq
- *     positions on the current device (16, 8, 4 or 2: the largest whose clusters all fit at
- *     once), or 0 when the kernel does not apply: head_dim other than 64 or 128,
+ *     positions on the current device (2 to 16: the largest whose clusters all fit at once),
+ *     or 0 when the kernel does not apply: head_dim other than 64 or 128,
  *     n_heads / n_kv_heads other than 1, 2, 4 or 8, or too many sequences.
  *   - chunks is 1 to 16; Q3_ERR_SHAPE if one cluster of that size (with its chunk's scores in
  *     shared memory) does not fit on the device. With batch > 1 the sequences must have separate

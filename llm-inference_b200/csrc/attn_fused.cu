@@ -531,7 +531,7 @@ unsigned take_error_attn_fused() {
 }
 
 // Chunks (CTAs per cluster) per (sequence, kv head) for `batch` sequences of up to max_seq
-// positions: the largest of 16, 8, 4, 2 whose clusters all fit on the device at once, or 0 when the
+// positions: the largest size up to 16 whose clusters all fit on the device at once, or 0 when the
 // fused kernel does not apply (head_dim other than 64 / 128, group size other than 1, 2, 4, 8, or
 // too many sequences for clusters of two: the split-KV path is the better fit there).
 int fused_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_seq) {
@@ -540,7 +540,7 @@ int fused_chunks(int batch, int n_heads, int n_kv_heads, int head_dim, int max_s
     const void *k = fused_kernel_for(nrep, head_dim);
     if (!k) return 0;
     const long long groups = (long long)batch * n_kv_heads;
-    for (int C = FA_MAX_CLUSTER; C >= 2; C /= 2)
+    for (int C = FA_MAX_CLUSTER; C >= 2; C--)
         if (fused_clusters(k, C, fused_smem_bytes(nrep, head_dim, chunk_cap(max_seq, C))) >= groups) return C;
     return 0;
 }

@@ -244,6 +244,7 @@ class Bench:
         f = lambda s: self.lib.call("q3_rope_attention_batched", out.data_ptr(), q.data_ptr(), k.data_ptr(),
                                     v.data_ptr(), qn.data_ptr(), kn.data_ptr(), kc.data_ptr(), vc.data_ptr(), *strides,
                                     pos.data_ptr(), B, nq, nkv, hd, max_seq, 1e-6, s_.rope_theta, scale, chunks, s)
+        self.extra = {"chunks": chunks}
         # K and V rows of positions 0..L-2 read, q/k/v read, the output and two cache rows written
         return f, B * (L - 1) * nkv * hd * 2 * 2 + B * (2 * nq + 4 * nkv) * hd * 2
 
@@ -265,6 +266,7 @@ def main(argv=None):
     q3 = sys.modules["llm_inference_b200"]
     for name in args.kernels:
         for B in args.batch:
+            b.extra = {}
             made = getattr(b, "k_" + name)(B)
             if made is None:
                 print(json.dumps({"kernel": name, "model": args.model, "batch": B, "skipped": "not applicable"}),
@@ -277,7 +279,7 @@ def main(argv=None):
                 raise SystemExit(f"{name} batch {B}: device error flags set")
             print(json.dumps({"kernel": name, "model": args.model, "batch": B, "us": round(us, 2),
                               "algorithmic_bytes": int(nbytes), "gbs": round(gbs, 1), "peak_gbs": peak,
-                              "frac": round(gbs / peak, 4), "peak_source": source}), flush=True)
+                              "frac": round(gbs / peak, 4), "peak_source": source, **b.extra}), flush=True)
             b.torch.cuda.empty_cache()
 
 
