@@ -34,6 +34,9 @@ namespace {
 __device__ unsigned g_dev_error;
 
 constexpr int GV_THREADS = 256;  // 8 warps per CTA
+#ifndef Q3_GEMV_LONG_ROWS
+#define Q3_GEMV_LONG_ROWS 1
+#endif
 // UR: chunk rounds (one 16-byte chunk per lane each) per batch and row; a unit's batch holds
 // RPU * UR chunks per lane. The host picks the smallest UR in {8, 12, 16} that covers a row in
 // one batch, else 16 (8 for gate_up, whose batches hold two rows).
@@ -75,13 +78,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
     return v;
 }
 
-template <int EPI, int UR, bool NORM>
-__global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant__ GemvArgs a) {
+template <int EPI, int UR, bool NORM, int THREADS>
+__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    static_assert(!NORM || THREADS == 256, "the rmsnorm order is the reference's 256-thread block");
     constexpr int RPU = EPI == GATE_UP ? 2 : 1;  // weight rows per output unit
     extern __shared__ __align__(16) bf16 xs[];    // NORM: [cols], the norm weight, then the normed x
-    __shared__ float warp_sums[GV_THREADS / 32];
+    __shared__ float warp_sums[THREADS / 32];
     const int lane = threadIdx.x % 32;
-    const int nw = gridDim.x * (GV_THREADS / 32);
+    const int nw = gridDim.x * (THREADS / 32);
     const int n_vec = a.cols / 8;
     const uint64_t policy = policy_evict_first();
     uint4 w[RPU][UR];
@@ -98,15 +102,15 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
         }
     };
 
-    int u = blockIdx.x * (GV_THREADS / 32) + threadIdx.x / 32;
+    int u = blockIdx.x * (THREADS / 32) + threadIdx.x / 32;
     pdl_trigger();
     if (u < a.units) load_batch(u, 0);
     if (NORM)
-        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) xs[i] = a.norm_w[i];
+        for (int i = threadIdx.x; i < a.cols; i += THREADS) xs[i] = a.norm_w[i];
     pdl_wait();
     if (NORM) {
         float sum = 0.0f;
-        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) {
+        for (int i = threadIdx.x; i < a.cols; i += THREADS) {
             const float v = __bfloat162float(a.x[i]);
             sum = __fmaf_rn(v, v, sum);
         }
@@ -115,9 +119,9 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
         __syncthreads();
         float total = 0.0f;
 #pragma unroll
-        for (int w_ = 0; w_ < GV_THREADS / 32; w_++) total += warp_sums[w_];
+        for (int w_ = 0; w_ < THREADS / 32; w_++) total += warp_sums[w_];
         const float inv_rms = rsqrtf(total / a.cols + a.eps);
-        for (int i = threadIdx.x; i < a.cols; i += GV_THREADS) {  // each thread rewrites its own elements
+        for (int i = threadIdx.x; i < a.cols; i += THREADS) {  // each thread rewrites its own elements
             const bf16 normed = __float2bfloat16(__bfloat162float(a.x[i]) * inv_rms);
             xs[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(xs[i]));
         }
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(GV_THREADS) gemv_kernel(const __grid_constant_
 
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int EPI, int UR, bool NORM>
+template <int EPI, int UR, bool NORM, int THREADS = GV_THREADS>
 int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     static int per_sm[64] = {};  // resident CTAs per SM, by device
     int dev = 0;
@@ -183,16 +187,16 @@ int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     const size_t smem = NORM ? (size_t)a.cols * 2 : 0, smem_plan = NORM ? (size_t)GV_NORM_MAX_COLS * 2 : 0;
     if (per_sm[dev] == 0) {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM>, GV_THREADS, smem_plan) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM, THREADS>, THREADS, smem_plan) !=
                 cudaSuccess ||
             n < 1)
             n = 1;
         cudaGetLastError();
         per_sm[dev] = n;
     }
-    const long long want = (a.units + GV_THREADS / 32 - 1) / (GV_THREADS / 32);
+    const long long want = (a.units + THREADS / 32 - 1) / (THREADS / 32);
     const int grid = (int)std::min<long long>(want, (long long)num_sms() * per_sm[dev]);
-    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM>, dim3(grid), dim3(GV_THREADS), smem, stream, 1, a));
+    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM, THREADS>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
     return Q3_OK;
 }
 
@@ -209,8 +213,16 @@ int launch_gemv(GemvArgs a, cudaStream_t stream) {
     const int rounds = (a.cols / 8 + 31) / 32;
     if (rounds <= 8) return launch_gemv_ur<EPI, 8>(a, stream);
     if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
-    if constexpr (EPI == GATE_UP) return launch_gemv_ur<EPI, 8>(a, stream);  // two rows: 16 chunks a batch
-    else return launch_gemv_ur<EPI, 16>(a, stream);
+    if constexpr (EPI == GATE_UP) {
+        return launch_gemv_ur<EPI, 8>(a, stream);  // two rows: 16 chunks a batch
+    } else {
+#if Q3_GEMV_LONG_ROWS
+        // long rows (down_proj: 38 rounds): 20 chunks per lane in flight, two batches a row instead
+        // of three; 4-warp CTAs keep enough warps resident (about 20 per SM) for one row each
+        if (rounds > 16 && rounds <= 40 && !a.norm_w) return launch_gemv_ur<EPI, 20, false, 128>(a, stream);
+#endif
+        return launch_gemv_ur<EPI, 16>(a, stream);
+    }
 }
 
 }  // namespace
