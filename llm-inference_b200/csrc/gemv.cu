@@ -8,8 +8,8 @@
 // the last is a multiple of 32 chunks.
 //
 // Memory pipeline (what is new): persistent warps, each owning output rows w, w + W, ... (W =
-// warps of the grid, sized to what is resident). The eight warps of a CTA take eight consecutive
-// rows, so each SM streams contiguous slabs of the matrix: measured faster, chained in a decode
+// warps of the grid, sized to what is resident). The warps of a CTA take consecutive rows, so
+// each SM streams contiguous slabs of the matrix: measured faster, chained in a decode
 // step, than spreading every SM's rows over the whole matrix to even out the rows per SM. A warp loads up to GV_U 16-byte chunks per lane
 // of its row at once (8 KB of one row per warp in flight) with streaming loads that bypass L1
 // and are marked evict-first in L2, then runs the reference's FMA chain over them. The first
@@ -33,7 +33,11 @@ namespace {
 
 __device__ unsigned g_dev_error;
 
-constexpr int GV_THREADS = 256;  // 8 warps per CTA
+// Threads per CTA. The residual projections (o_proj, down) run 4-warp CTAs, measured faster than 8
+// in the chained batch-1 step (the next kernel's CTAs take an SM's slots as soon as a few warps of
+// the previous one are done); the others keep 8, where the in-kernel rmsnorm costs per CTA.
+constexpr int GV_THREADS = 256;
+constexpr int GV_THREADS_RESIDUAL = 128;
 #ifndef Q3_GEMV_LONG_ROWS
 #define Q3_GEMV_LONG_ROWS 1
 #endif
@@ -78,12 +82,14 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
     return v;
 }
 
-template <int EPI, int UR, bool NORM, int THREADS>
-__global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gemv_kernel(const __grid_constant__ GemvArgs a) {
-    static_assert(!NORM || THREADS == 256, "the rmsnorm order is the reference's 256-thread block");
+template <int EPI, int UR, bool NORM, int THREADS, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    constexpr int REF = 256;                      // the reference rmsnorm's block
+    constexpr int NREF = REF / THREADS;           // reference threads each thread stands in for
+    static_assert(REF % THREADS == 0, "the rmsnorm order needs a divisor of 256 threads");
     constexpr int RPU = EPI == GATE_UP ? 2 : 1;  // weight rows per output unit
     extern __shared__ __align__(16) bf16 xs[];    // NORM: [cols], the norm weight, then the normed x
-    __shared__ float warp_sums[THREADS / 32];
+    __shared__ float warp_sums[REF / 32];
     const int lane = threadIdx.x % 32;
     const int nw = gridDim.x * (THREADS / 32);
     const int n_vec = a.cols / 8;
@@ -109,17 +115,28 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gemv_kernel(c
         for (int i = threadIdx.x; i < a.cols; i += THREADS) xs[i] = a.norm_w[i];
     pdl_wait();
     if (NORM) {
-        float sum = 0.0f;
-        for (int i = threadIdx.x; i < a.cols; i += THREADS) {
-            const float v = __bfloat162float(a.x[i]);
-            sum = __fmaf_rn(v, v, sum);
+        // reference thread r = threadIdx.x + k * THREADS sums x[r], x[r + 256], ... (accumulator k)
+        float sum[NREF];
+#pragma unroll
+        for (int k = 0; k < NREF; k++) sum[k] = 0.0f;
+        for (int i0 = 0; i0 < a.cols; i0 += REF)
+#pragma unroll
+            for (int k = 0; k < NREF; k++) {
+                const int i = i0 + threadIdx.x + k * THREADS;
+                if (i < a.cols) {
+                    const float v = __bfloat162float(a.x[i]);
+                    sum[k] = __fmaf_rn(v, v, sum[k]);
+                }
+            }
+#pragma unroll
+        for (int k = 0; k < NREF; k++) {  // reference warp threadIdx.x / 32 + k * THREADS / 32
+            for (int off = 16; off > 0; off >>= 1) sum[k] += __shfl_xor_sync(0xffffffffu, sum[k], off);
+            if (lane == 0) warp_sums[threadIdx.x / 32 + k * (THREADS / 32)] = sum[k];
         }
-        for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-        if (lane == 0) warp_sums[threadIdx.x / 32] = sum;
         __syncthreads();
         float total = 0.0f;
 #pragma unroll
-        for (int w_ = 0; w_ < THREADS / 32; w_++) total += warp_sums[w_];
+        for (int w_ = 0; w_ < REF / 32; w_++) total += warp_sums[w_];
         const float inv_rms = rsqrtf(total / a.cols + a.eps);
         for (int i = threadIdx.x; i < a.cols; i += THREADS) {  // each thread rewrites its own elements
             const bf16 normed = __float2bfloat16(__bfloat162float(a.x[i]) * inv_rms);
@@ -177,8 +194,9 @@ __global__ void __launch_bounds__(THREADS, THREADS == 128 ? 5 : 1) gemv_kernel(c
 
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int EPI, int UR, bool NORM, int THREADS = GV_THREADS>
+template <int EPI, int UR, bool NORM, int MINB = 1>
 int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
+    constexpr int THREADS = EPI == RESIDUAL ? GV_THREADS_RESIDUAL : GV_THREADS;
     static int per_sm[64] = {};  // resident CTAs per SM, by device
     int dev = 0;
     cudaGetDevice(&dev);
@@ -187,7 +205,8 @@ int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     const size_t smem = NORM ? (size_t)a.cols * 2 : 0, smem_plan = NORM ? (size_t)GV_NORM_MAX_COLS * 2 : 0;
     if (per_sm[dev] == 0) {
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM, THREADS>, THREADS, smem_plan) !=
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM, THREADS, MINB>, THREADS,
+                                                          smem_plan) !=
                 cudaSuccess ||
             n < 1)
             n = 1;
@@ -196,7 +215,7 @@ int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     }
     const long long want = (a.units + THREADS / 32 - 1) / (THREADS / 32);
     const int grid = (int)std::min<long long>(want, (long long)num_sms() * per_sm[dev]);
-    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM, THREADS>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
+    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM, THREADS, MINB>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
     return Q3_OK;
 }
 
@@ -213,14 +232,17 @@ int launch_gemv(GemvArgs a, cudaStream_t stream) {
     const int rounds = (a.cols / 8 + 31) / 32;
     if (rounds <= 8) return launch_gemv_ur<EPI, 8>(a, stream);
     if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
+    if constexpr (EPI == RESIDUAL) {
+        if (rounds <= 16) return launch_gemv_ur<EPI, 16, false, 5>(a, stream);
+#if Q3_GEMV_LONG_ROWS
+        // long rows (down_proj: 38 rounds): 20 chunks per lane in flight, two batches a row instead
+        // of three; at most 102 registers keep 5 CTAs (20 warps) per SM, one row per warp
+        if (rounds <= 40) return launch_gemv_ur<EPI, 20, false, 5>(a, stream);
+#endif
+    }
     if constexpr (EPI == GATE_UP) {
         return launch_gemv_ur<EPI, 8>(a, stream);  // two rows: 16 chunks a batch
     } else {
-#if Q3_GEMV_LONG_ROWS
-        // long rows (down_proj: 38 rounds): 20 chunks per lane in flight, two batches a row instead
-        // of three; 4-warp CTAs keep enough warps resident (about 20 per SM) for one row each
-        if (rounds > 16 && rounds <= 40 && !a.norm_w) return launch_gemv_ur<EPI, 20, false, 128>(a, stream);
-#endif
         return launch_gemv_ur<EPI, 16>(a, stream);
     }
 }
