@@ -177,8 +177,21 @@ def shape_from_config(cfg: dict) -> Qwen3Shape:
     return s
 
 
-def read_checkpoint(model_dir) -> tuple[Qwen3Shape, dict[str, np.ndarray]]:
-    """Read and validate a checkpoint directory; tensors are bf16 bit arrays."""
+@dataclass
+class TensorSpan:
+    """Where one tensor's bytes lie: `nbytes` bytes at byte `offset` of file `path`."""
+    path: Path
+    offset: int
+    nbytes: int
+    shape: tuple[int, ...]
+
+
+def checkpoint_layout(model_dir) -> tuple[Qwen3Shape, dict[str, TensorSpan]]:
+    """Validate a checkpoint directory from its config files and safetensors headers alone (the
+    tensor data is not read) and locate every tensor the engine uses. The checks are those of
+    src/loader.cu:113-140 and :313-380: config fields, an eos token, BF16 dtype, shapes implied
+    by config.json, data offsets inside the file, 16-byte alignment, no unused tensors (a tied
+    checkpoint may carry lm_head.weight)."""
     d = Path(model_dir)
     s = shape_from_config(json.loads((d / "config.json").read_text()))
     gen = json.loads((d / "generation_config.json").read_text())
@@ -191,37 +204,51 @@ def read_checkpoint(model_dir) -> tuple[Qwen3Shape, dict[str, np.ndarray]]:
         raise CheckpointError(f"no .safetensors files in {d}")
     entries = {}
     for p in files:
-        raw = p.read_bytes()
-        if len(raw) < 8:
-            raise CheckpointError(f"{p}: too small to be a safetensors file")
-        (n,) = struct.unpack("<Q", raw[:8])
-        if n > len(raw) - 8:
-            raise CheckpointError(f"{p}: bad header length")
-        header = json.loads(raw[8:8 + n])
-        data = memoryview(raw)[8 + n:]
+        size = p.stat().st_size
+        with open(p, "rb") as f:
+            head = f.read(8)
+            if len(head) < 8:
+                raise CheckpointError(f"{p}: too small to be a safetensors file")
+            (n,) = struct.unpack("<Q", head)
+            if n > size - 8:
+                raise CheckpointError(f"{p}: bad header length")
+            header = json.loads(f.read(n))
         for name, meta in header.items():
             if name != "__metadata__":
-                entries[name] = (meta, data)
+                entries[name] = (meta, p, 8 + n, size - 8 - n)
     want = tensor_shapes(s)
-    tensors = {}
+    spans = {}
     for name, shape in want.items():
         if name not in entries:
             raise CheckpointError(f"tensor {name} not found")
-        meta, data = entries[name]
+        meta, path, data_start, data_len = entries[name]
         if meta.get("dtype") != "BF16":
             raise CheckpointError(f"{name}: dtype is not BF16")
         if tuple(meta["shape"]) != shape:
             raise CheckpointError(f"{name}: shape {meta['shape']}, config.json implies {list(shape)}")
         b, e = meta["data_offsets"]
-        if e > len(data) or e - b != int(np.prod(shape)) * 2:
+        if e > data_len or e - b != int(np.prod(shape)) * 2:
             raise CheckpointError(f"{name}: data_offsets do not match its shape")
         if b % 16:
             raise CheckpointError(f"{name}: offset {b} is not 16-byte aligned")
-        tensors[name] = np.frombuffer(data[b:e], dtype=np.uint16).reshape(shape)
+        spans[name] = TensorSpan(path, data_start + b, e - b, shape)
     allowed = 1 if (s.tie_word_embeddings and "lm_head.weight" in entries) else 0
-    unused = len(entries) - len(tensors)
+    unused = len(entries) - len(spans)
     if unused != allowed:
         raise CheckpointError(f"{unused} tensors in the safetensors files are not used by the engine")
+    return s, spans
+
+
+def read_checkpoint(model_dir) -> tuple[Qwen3Shape, dict[str, np.ndarray]]:
+    """Read and validate a checkpoint directory; tensors are bf16 bit arrays (views of the
+    memory-mapped files)."""
+    s, spans = checkpoint_layout(model_dir)
+    maps = {}
+    tensors = {}
+    for name, sp in spans.items():
+        if sp.path not in maps:
+            maps[sp.path] = np.memmap(sp.path, dtype=np.uint8, mode="r")
+        tensors[name] = maps[sp.path][sp.offset:sp.offset + sp.nbytes].view(np.uint16).reshape(sp.shape)
     return s, tensors
 
 

@@ -101,6 +101,48 @@ class DeviceWeights:
         return cls.from_tensors(shape, tensors, device)
 
     @classmethod
+    def load(cls, model_dir, device="cuda", staging_bytes: int = 64 << 20):
+        """from_checkpoint's result (the same device layout, bit for bit) without its host copies.
+
+        The reference uploads each shard with one synchronous pageable cudaMemcpy after reading
+        the whole file (src/loader.cu:143-180). Here the safetensors headers are validated first
+        (checkpoint_layout), the files are memory-mapped, and every tensor streams through two
+        pinned staging buffers: while one buffer's chunk is copied to the device
+        (cudaMemcpyAsync on a dedicated stream), the next chunk is paged in and copied into the
+        other, so disk or page-cache reads overlap the DMA. Returns once the weights are on the
+        device."""
+        import torch
+        shape, spans = ckpt.checkpoint_layout(model_dir)
+        _, offsets, total = cls._layout(shape)
+        blob = torch.zeros(total // 2, dtype=torch.int16, device=device)  # padding bytes are zero
+        obj = cls(shape, blob, offsets)
+        dst = blob.view(torch.uint8)
+        stream = torch.cuda.Stream(device=dst.device)
+        stream.wait_stream(torch.cuda.current_stream(dst.device))  # after the zero fill
+        stage = [torch.empty(staging_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+        stage_np = [t.numpy() for t in stage]
+        done = [None, None]
+        maps = {}
+        k = 0
+        for name, sp in sorted(spans.items(), key=lambda kv: (str(kv[1].path), kv[1].offset)):  # file order
+            if sp.path not in maps:
+                maps[sp.path] = np.memmap(sp.path, dtype=np.uint8, mode="r")
+            src = maps[sp.path]
+            for c0 in range(0, sp.nbytes, staging_bytes):
+                n = min(staging_bytes, sp.nbytes - c0)
+                buf = k % 2
+                if done[buf] is not None:
+                    done[buf].synchronize()  # the buffer's previous chunk has reached the device
+                np.copyto(stage_np[buf][:n], src[sp.offset + c0:sp.offset + c0 + n])
+                with torch.cuda.stream(stream):
+                    dst[offsets[name] + c0:offsets[name] + c0 + n].copy_(stage[buf][:n], non_blocking=True)
+                    done[buf] = torch.cuda.Event()
+                    done[buf].record(stream)
+                k += 1
+        stream.synchronize()
+        return obj
+
+    @classmethod
     def random(cls, shape: ckpt.Qwen3Shape, seed: int = 0, device="cuda"):
         """Random-init weights generated on the device (linear N(0, 0.02), norms 1 + N(0, 0.02)),
         one generator stream per tensor in sorted-name order."""

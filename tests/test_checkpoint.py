@@ -1,0 +1,99 @@
+"""Checkpoint layout and validation (checkpoint.py), the rules of the reference's loader
+(src/loader.cu:113-140, :313-380), on CPU; and the fast device loader against the plain one on a
+B200.
+
+- A written random checkpoint reads back bit for bit through the header-only layout and the
+  memory-mapped reader.
+- Each malformed checkpoint raises CheckpointError: missing tensor, wrong dtype, wrong shape,
+  misaligned data, an unused tensor, no eos token.
+"""
+import json
+import struct
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+import conftest  # noqa: E402,F401
+
+from llm_inference_b200 import checkpoint as ckpt  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def tiny(tmp_path_factory):
+    d = tmp_path_factory.mktemp("ckpt")
+    ckpt.write_random_checkpoint(d, "tiny", seed=3)
+    return d
+
+
+def test_layout_and_reader_round_trip(tiny):
+    shape, spans = ckpt.checkpoint_layout(tiny)
+    assert (shape.hidden_size, shape.num_hidden_layers) == (256, 2)
+    want = ckpt.random_tensors(ckpt.PRESETS["tiny"], seed=3)
+    assert set(spans) == set(want)
+    _, tensors = ckpt.read_checkpoint(tiny)
+    raw = (tiny / "model.safetensors").read_bytes()
+    for name, a in want.items():
+        assert tensors[name].shape == a.shape
+        assert np.array_equal(np.asarray(tensors[name]), np.asarray(a, np.uint16)), name
+        sp = spans[name]
+        assert sp.nbytes == a.size * 2
+        assert raw[sp.offset:sp.offset + sp.nbytes] == np.asarray(a, np.uint16).tobytes(), name
+
+
+def _rewrite(src: Path, dst: Path, edit_header=None, gen=None):
+    """Copy a checkpoint, optionally editing the safetensors header and generation_config.json."""
+    dst.mkdir()
+    raw = (src / "model.safetensors").read_bytes()
+    (n,) = struct.unpack("<Q", raw[:8])
+    header = json.loads(raw[8:8 + n])
+    data = raw[8 + n:]
+    if edit_header:
+        header, data = edit_header(header, data)
+    hb = json.dumps(header).encode()
+    hb += b" " * ((8 - len(hb) % 8) % 8)
+    (dst / "model.safetensors").write_bytes(struct.pack("<Q", len(hb)) + hb + data)
+    (dst / "config.json").write_text((src / "config.json").read_text())
+    g = json.loads((src / "generation_config.json").read_text()) if gen is None else gen
+    (dst / "generation_config.json").write_text(json.dumps(g))
+    return dst
+
+
+@pytest.mark.parametrize("case", ["missing", "dtype", "shape", "misaligned", "unused", "no_eos"])
+def test_malformed_checkpoints_are_rejected(tiny, tmp_path, case):
+    def edit(header, data):
+        name = next(k for k in sorted(header) if k.endswith("q_proj.weight"))
+        if case == "missing":
+            del header[name]
+        elif case == "dtype":
+            header[name]["dtype"] = "F16"
+        elif case == "shape":
+            r, c = header[name]["shape"]
+            header[name]["shape"] = [r // 2, c * 2]  # same number of elements, not config.json's shape
+        elif case == "misaligned":
+            b, e = header[name]["data_offsets"]
+            header[name]["data_offsets"] = [b + 2, e + 2]
+            data = data + b"\0\0"
+        elif case == "unused":
+            header["extra.weight"] = {"dtype": "BF16", "shape": [8], "data_offsets": [len(data), len(data) + 16]}
+            data = data + bytes(16)
+        return header, data
+
+    d = _rewrite(tiny, tmp_path / "bad", edit_header=None if case == "no_eos" else edit,
+                 gen={} if case == "no_eos" else None)
+    with pytest.raises(ckpt.CheckpointError):
+        ckpt.checkpoint_layout(d)
+
+
+@pytest.mark.gpu
+def test_fast_loader_matches_plain_loader(tiny):
+    torch = pytest.importorskip("torch")
+    from llm_inference_b200.engine import DeviceWeights
+    plain = DeviceWeights.from_checkpoint(tiny)
+    for staging in (64 << 20, 4096, 16000):  # one chunk per tensor, and chunks that split tensors
+        fast = DeviceWeights.load(tiny, staging_bytes=staging)
+        assert fast.offsets == plain.offsets
+        assert torch.equal(fast.blob, plain.blob), f"staging {staging}"
