@@ -59,6 +59,12 @@ int q3_last_cuda_error(void);
  * range). Synchronizes `stream` first. Returns a q3_status; the flags go to *flags. */
 int q3_device_error(void *stream, unsigned *flags);
 
+/* Self-test of the bounded waits the kernels use (no counterpart in the reference): launches one
+ * wait on an mbarrier phase that nothing completes. The wait gives up after its time limit (about
+ * two seconds), sets device flag bit 0 and returns; *done (device int) becomes 2. The context stays
+ * usable. Used by the failure-detection test; never part of a decode step. */
+int q3_selftest_wait_timeout(int *done, void *stream);
+
 /* ---------------------------------------------------------------------------------------
  * Drop-in launchers (batch 1). Each replaces the launcher of the same name without the
  * q3_ prefix in src/kernels.cuh, with identical parameters.
@@ -181,7 +187,9 @@ int q3_attention_batched(q3_bf16 *out, const q3_bf16 *q, const q3_bf16 *key_cach
  *   - Shapes whose scratch (q3_attention_scratch_bytes) exceeds the array return
  *     Q3_ERR_SCRATCH_LIMIT and launch nothing.
  *   - The first call on a device looks up the array's device address (once per device, with
- *     that device current); make that first call before any stream capture.
+ *     that device current); make that first call before any stream capture. The address is kept
+ *     per device and CUDA context: after a cudaDeviceReset the next call looks it up again, so
+ *     that call too should come before any capture.
  *   - Every call on a device shares the one array. Calls that overlap on the GPU (other
  *     streams, other host threads) race on it; serialize them. Nothing in the array needs
  *     clearing between calls: each call writes every scratch value before using it. */

@@ -29,6 +29,7 @@ SIGNATURES: dict[str, list] = {
     "q3_status_string": [_I],
     "q3_last_cuda_error": [],
     "q3_device_error": [_P, ctypes.POINTER(_U)],
+    "q3_selftest_wait_timeout": [_P, _P],
     "q3_embedding_forward": [_P, _P, _P, _I, _P],
     "q3_rmsnorm_forward": [_P, _P, _P, _I, _I, _F, _P],
     "q3_gemv_forward": [_P, _P, _P, _I, _I, _P],

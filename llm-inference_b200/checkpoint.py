@@ -214,8 +214,11 @@ def checkpoint_layout(model_dir) -> tuple[Qwen3Shape, dict[str, TensorSpan]]:
                 raise CheckpointError(f"{p}: bad header length")
             header = json.loads(f.read(n))
         for name, meta in header.items():
-            if name != "__metadata__":
-                entries[name] = (meta, p, 8 + n, size - 8 - n)
+            if name == "__metadata__":
+                continue
+            if name in entries:  # the reference's lookup would take the first file's copy
+                raise CheckpointError(f"tensor {name} appears in both {entries[name][1].name} and {p.name}")
+            entries[name] = (meta, p, 8 + n, size - 8 - n)
     want = tensor_shapes(s)
     spans = {}
     for name, shape in want.items():
@@ -226,8 +229,12 @@ def checkpoint_layout(model_dir) -> tuple[Qwen3Shape, dict[str, TensorSpan]]:
             raise CheckpointError(f"{name}: dtype is not BF16")
         if tuple(meta["shape"]) != shape:
             raise CheckpointError(f"{name}: shape {meta['shape']}, config.json implies {list(shape)}")
-        b, e = meta["data_offsets"]
-        if e > data_len or e - b != int(np.prod(shape)) * 2:
+        offs = meta.get("data_offsets")
+        if (not isinstance(offs, list) or len(offs) != 2
+                or not all(isinstance(o, int) and not isinstance(o, bool) for o in offs)):
+            raise CheckpointError(f"{name}: data_offsets must be two integers")
+        b, e = offs
+        if b < 0 or e > data_len or e - b != int(np.prod(shape)) * 2:
             raise CheckpointError(f"{name}: data_offsets do not match its shape")
         if b % 16:
             raise CheckpointError(f"{name}: offset {b} is not 16-byte aligned")

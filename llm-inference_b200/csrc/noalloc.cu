@@ -33,20 +33,41 @@ static __device__ __align__(256) unsigned char g_attn_scratch[Q3_ATTENTION_STATI
 constexpr int MAX_DEVICES = 64;
 std::mutex g_mu;
 void *g_addr[MAX_DEVICES] = {};
+void *g_ctx[MAX_DEVICES] = {};  // the context g_addr[dev] was looked up in
 
-// Device address of g_attn_scratch on the current device, looked up once per device (the
-// lookup can load the module on that device, so it is done outside any later call's capture).
+// The current context (CUcontext) through the driver entry point, so the library needs no -lcuda.
+void *current_context() {
+    typedef int (*GetCurrent)(void **);
+    static GetCurrent fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            return nullptr;
+        fn = reinterpret_cast<GetCurrent>(p);
+    }
+    void *ctx = nullptr;
+    return fn(&ctx) == 0 ? ctx : nullptr;
+}
+
+// Device address of g_attn_scratch on the current device, looked up once per device and context:
+// the first call on a device (and the first after a cudaDeviceReset, which replaces the context and
+// reloads the module at a possibly different address) does the lookup. The lookup can load the
+// module, so that first call should come before any stream capture.
 int scratch_address(void **out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return record_cuda_error(e);
     if (dev < 0 || dev >= MAX_DEVICES) return Q3_ERR_DEVICE;
+    void *ctx = current_context();
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_addr[dev]) {
+    if (!g_addr[dev] || ctx == nullptr || ctx != g_ctx[dev]) {
         void *p = nullptr;
         e = cudaGetSymbolAddress(&p, g_attn_scratch);
         if (e != cudaSuccess || !p) return record_cuda_error(e != cudaSuccess ? e : cudaErrorInvalidSymbol);
         g_addr[dev] = p;
+        g_ctx[dev] = current_context();  // the lookup made the device's context current if none was
     }
     *out = g_addr[dev];
     return Q3_OK;

@@ -160,6 +160,38 @@ class DeviceWeights:
     def tensor(self, name):
         return device_view(self.ptr[name], ckpt.tensor_shapes(self.shape)[name], "bf16")
 
+    def save(self, out_dir):
+        """Write these weights as a checkpoint directory in the reference's layout
+        (model.safetensors, config.json, generation_config.json; what src/loader.cu reads). The
+        device blob comes to the host in one copy and each tensor is written from its slice."""
+        import json
+        import struct
+        from pathlib import Path
+
+        out = Path(out_dir)
+        out.mkdir(parents=True, exist_ok=True)
+        shapes = ckpt.tensor_shapes(self.shape)
+        host = self.blob.view(-1).cpu().numpy().view(np.uint8)
+        header, off = {}, 0
+        names = sorted(shapes)
+        for name in names:
+            nbytes = int(np.prod(shapes[name])) * 2
+            if nbytes % 16:  # the reference loader wants 16-byte aligned offsets (src/loader.cu:273-275)
+                raise ValueError(f"{name}: {nbytes} bytes is not a multiple of 16")
+            header[name] = {"dtype": "BF16", "shape": list(shapes[name]), "data_offsets": [off, off + nbytes]}
+            off += nbytes
+        hb = json.dumps(header, separators=(",", ":")).encode()
+        hb += b" " * (-(len(hb) + 8) % 16)
+        with open(out / "model.safetensors", "wb") as f:
+            f.write(struct.pack("<Q", len(hb)))
+            f.write(hb)
+            for name in names:
+                o = self.offsets[name]
+                f.write(memoryview(host[o:o + header[name]["data_offsets"][1] - header[name]["data_offsets"][0]]))
+        (out / "config.json").write_text(json.dumps(ckpt.config_json(self.shape), indent=1))
+        (out / "generation_config.json").write_text(json.dumps({"eos_token_id": self.shape.eos_token_id}))
+        return out
+
     def q3_weights(self):
         s = self.shape
         layers = (Q3LayerWeights * s.num_hidden_layers)()

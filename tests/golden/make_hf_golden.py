@@ -1,7 +1,7 @@
 """Generate tests/golden/hf_tiny/: the reference's Hugging Face harness run on a tiny model.
 
 Run in the development container, where the reference tree is mounted (default
-/root/reference, or $LLM_INFERENCE_REF). It imports the reference's own hook set and wiring
+$LLM_INFERENCE_REF, else the "reference" directory beside this repository). It imports the reference's own hook set and wiring
 check (ref/dump.py: ``install_hooks``, ``check_wiring``) and runs Hugging Face Qwen3 in bf16
 with eager attention on the CPU, as ref/calibrate.py does. Outputs:
 
@@ -29,7 +29,7 @@ sys.path.insert(0, str(ROOT / "tests"))
 import conftest  # noqa: E402  (loads the package)
 from llm_inference_b200 import checkpoint  # noqa: E402
 
-REF = Path(os.environ.get("LLM_INFERENCE_REF", "/root/reference"))
+REF = Path(os.environ.get("LLM_INFERENCE_REF", str(Path(__file__).resolve().parents[3] / "reference")))
 sys.path.insert(0, str(REF / "ref"))
 from dump import check_wiring, install_hooks  # noqa: E402  (the reference's harness)
 

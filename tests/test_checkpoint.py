@@ -5,7 +5,8 @@ B200.
 - A written random checkpoint reads back bit for bit through the header-only layout and the
   memory-mapped reader.
 - Each malformed checkpoint raises CheckpointError: missing tensor, wrong dtype, wrong shape,
-  misaligned data, an unused tensor, no eos token.
+  misaligned data, an unused tensor, no eos token, a negative or non-integer data offset (which
+  would otherwise read the header as weights), and one tensor name in two shards.
 """
 import json
 import struct
@@ -62,7 +63,8 @@ def _rewrite(src: Path, dst: Path, edit_header=None, gen=None):
     return dst
 
 
-@pytest.mark.parametrize("case", ["missing", "dtype", "shape", "misaligned", "unused", "no_eos"])
+@pytest.mark.parametrize("case", ["missing", "dtype", "shape", "misaligned", "unused", "no_eos", "negative_offset",
+                                  "float_offset"])
 def test_malformed_checkpoints_are_rejected(tiny, tmp_path, case):
     def edit(header, data):
         name = next(k for k in sorted(header) if k.endswith("q_proj.weight"))
@@ -77,6 +79,13 @@ def test_malformed_checkpoints_are_rejected(tiny, tmp_path, case):
             b, e = header[name]["data_offsets"]
             header[name]["data_offsets"] = [b + 2, e + 2]
             data = data + b"\0\0"
+        elif case == "negative_offset":  # 16-byte aligned, right length, but before the data
+            b, e = header[name]["data_offsets"]
+            n = e - b
+            header[name]["data_offsets"] = [-16, n - 16]
+        elif case == "float_offset":
+            b, e = header[name]["data_offsets"]
+            header[name]["data_offsets"] = [float(b), float(e)]
         elif case == "unused":
             header["extra.weight"] = {"dtype": "BF16", "shape": [8], "data_offsets": [len(data), len(data) + 16]}
             data = data + bytes(16)
@@ -86,6 +95,42 @@ def test_malformed_checkpoints_are_rejected(tiny, tmp_path, case):
                  gen={} if case == "no_eos" else None)
     with pytest.raises(ckpt.CheckpointError):
         ckpt.checkpoint_layout(d)
+
+
+def test_tensor_in_two_shards_is_rejected(tiny, tmp_path):
+    """Split the checkpoint into two shards that both hold one tensor."""
+    raw = (tiny / "model.safetensors").read_bytes()
+    (n,) = struct.unpack("<Q", raw[:8])
+    header = json.loads(raw[8:8 + n])
+    data = raw[8 + n:]
+    names = sorted(k for k in header if k != "__metadata__")
+    dup = names[0]
+
+    def shard(keys):
+        h, blob = {}, b""
+        for k in keys:
+            b, e = header[k]["data_offsets"]
+            pad = (-len(blob)) % 16
+            blob += bytes(pad)
+            h[k] = dict(header[k], data_offsets=[len(blob), len(blob) + e - b])
+            blob += data[b:e]
+        hb = json.dumps(h).encode()
+        hb += b" " * ((8 - len(hb) % 8) % 8)
+        return struct.pack("<Q", len(hb)) + hb + blob
+
+    d = tmp_path / "two"
+    d.mkdir()
+    half = len(names) // 2
+    (d / "model-00001-of-00002.safetensors").write_bytes(shard(names[:half]))
+    (d / "model-00002-of-00002.safetensors").write_bytes(shard(names[half:] + [dup]))
+    for f in ("config.json", "generation_config.json"):
+        (d / f).write_text((tiny / f).read_text())
+    with pytest.raises(ckpt.CheckpointError, match="appears in both"):
+        ckpt.checkpoint_layout(d)
+    # the same two shards without the duplicate load
+    (d / "model-00002-of-00002.safetensors").write_bytes(shard(names[half:]))
+    shape, spans = ckpt.checkpoint_layout(d)
+    assert set(spans) == set(names)
 
 
 @pytest.mark.gpu

@@ -7,6 +7,8 @@ oracle/_ref/ref_engine).
 On a random-init tiny checkpoint in the reference's layout the two must print identical weight
 checksums (--checksums), identical greedy tokens (--max-new, graph mode) and bit-identical
 activation dumps of every layer (--dump: 17 tensors per layer plus embed, final_norm, logits).
+On a Qwen3-4B-shaped checkpoint both run the reference's --bench protocol and print the same
+tokens; their rates are recorded (printed at the end of the run).
 """
 import subprocess
 import sys
@@ -71,6 +73,36 @@ def test_layer_dumps_bit_identical(setup):
         a = np.fromfile(da / name, dtype=np.float32)
         b = np.fromfile(db / name, dtype=np.float32)
         assert a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32)), name
+
+
+def _bench(binary, model, tokens, steps, runs):
+    r = run(binary, model, "--tokens", tokens, "--bench", steps, "--runs", runs, timeout=900)
+    secs = [float(line.split()[3]) for line in r.stdout.splitlines() if line.startswith("run ")]
+    assert len(secs) == runs
+    return sorted(steps / s for s in secs)[runs // 2]
+
+
+def test_bench_qwen3_4b_against_reference_kernels(tmp_path):
+    """Both programs on a random Qwen3-4B checkpoint written from device weights, --bench 128."""
+    if not DROPIN.exists() or not REF_ENGINE.exists():
+        pytest.skip("drop-in or reference engine not built")
+    torch = pytest.importorskip("torch")
+    import parity
+    from llm_inference_b200.engine import DeviceWeights
+    w = DeviceWeights.random(checkpoint.PRESETS["qwen3-4b"], seed=0)
+    torch.cuda.synchronize()
+    model = w.save(tmp_path / "model4b")
+    del w
+    torch.cuda.empty_cache()
+    tokens = tmp_path / "tokens.txt"
+    tokens.write_text("17\n")
+    mine = _bench(DROPIN, model, tokens, 128, 3)
+    ref = _bench(REF_ENGINE, model, tokens, 128, 3)
+    parity.MEASURES.append(f"drop-in --bench 128 at Qwen3-4B: this library {mine:.1f} tok/s, "
+                           f"reference kernels {ref:.1f} tok/s ({mine / ref:.2f}x)")
+    a = run(DROPIN, model, "--tokens", tokens, "--max-new", 8, timeout=900).stdout.split()
+    b = run(REF_ENGINE, model, "--tokens", tokens, "--max-new", 8, timeout=900).stdout.split()
+    assert a == b
 
 
 def test_bench_mode_runs(setup):

@@ -1,0 +1,209 @@
+"""Parity at the shapes the benchmarks run, against the reference's own kernels.
+
+The other GPU tests pin each kernel on small and medium shapes. These run the benchmarked
+configurations themselves, with the reference's src/kernels.cu compiled for sm_100a
+(oracle/_ref/libqwen3_ref.so) as the oracle:
+  - config 4's attention: 32 sequences, 32 query / 8 kv heads, head_dim 128, positions spread
+    over 3900..4200, head-major caches poisoned with NaN past each position, through
+    q3_attention_batched (split-KV, tcgen05 scores and P.V);
+  - config 3's far end: one sequence at position 8191 (past the reference engine's MAX_SEQ of
+    4096, src/forward.cu:8, which its kernels do not depend on), through the split path and the
+    fused RoPE + attention launch the batch-1 engine uses;
+  - config 4's engine: a Qwen3-4B-shaped model cut to 2 layers, 32 sequences, every cache
+    pre-filled with N(0,1) to position 4096, 16 greedy steps through the captured batched engine
+    (tcgen05 projections, split attention), teacher-forced with the reference's tokens. At every
+    step the engine's argmax must equal the reference's wherever the reference's top-2 logit gap
+    exceeds 1e-2, and its logits must stay within a few ulps (the bar is in the test).
+The bar is tests/parity.check_close; every comparison's max-ulp figure is printed at the end of
+the run.
+"""
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE))
+sys.path.insert(0, str(HERE / "golden"))
+import conftest  # noqa: E402,F401
+import oracle as O  # noqa: E402
+import ref_kernels  # noqa: E402
+from parity import attention_abs_terms, bits, check_close, check_equal, record  # noqa: E402
+
+torch = pytest.importorskip("torch")
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not ref_kernels.available(), reason="reference kernels not built (oracle/Makefile ref)")]
+
+import llm_inference_b200 as q3  # noqa: E402
+from llm_inference_b200 import _lib, checkpoint  # noqa: E402
+from llm_inference_b200.engine import DeviceWeights, Engine  # noqa: E402
+
+EPS, THETA = 1e-6, 1e6
+
+
+def rn(g, *shape, std=1.0, mean=0.0):
+    return (torch.randn(*shape, generator=g, device="cuda") * std + mean).bfloat16()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def head_major(cache, n_kv, hd):
+    b, t, _ = cache.shape
+    return cache.view(b, t, n_kv, hd).permute(0, 2, 1, 3).contiguous()
+
+
+def ref_attention(q, kc, vc, positions, n_heads, n_kv, hd, max_seq, scale):
+    """The reference's attention_forward per sequence on [B][max_seq][n_kv*hd] caches."""
+    out = torch.empty_like(q)
+    att = torch.empty(n_heads * max_seq, dtype=torch.float32, device="cuda")
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    for b in range(q.shape[0]):
+        ref_kernels.call("attention_forward", out[b].data_ptr(), q[b].data_ptr(), kc[b].data_ptr(), vc[b].data_ptr(),
+                         att.data_ptr(), n_heads, n_kv, hd, pos[b:b + 1].data_ptr(), max_seq, scale, stream())
+    torch.cuda.synchronize()
+    return out
+
+
+def split_attention(q, kc_head, vc_head, positions, n_heads, n_kv, hd, max_seq, scale):
+    batch = q.shape[0]
+    out = torch.full_like(q, float("nan"))
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    nbytes = _lib.load().q3_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), kc_head.data_ptr(), vc_head.data_ptr(),
+              n_kv * max_seq * hd, hd, max_seq * hd, scratch.data_ptr(), pos.data_ptr(), batch, n_heads, n_kv, hd,
+              max_seq, scale, stream())
+    torch.cuda.synchronize()
+    return out
+
+
+def poisoned_caches(g, batch, max_seq, kvd, positions):
+    kc, vc = rn(g, batch, max_seq, kvd), rn(g, batch, max_seq, kvd)
+    for b, p in enumerate(positions):
+        kc[b, p + 1:] = float("nan")
+        vc[b, p + 1:] = float("nan")
+    return kc, vc
+
+
+def test_split_attention_at_config4_shape():
+    """32 sequences at positions 3900..4200, the benchmark's attention launch."""
+    batch, n_heads, n_kv, hd, max_seq = 32, 32, 8, 128, 4224
+    positions = np.linspace(3900, 4200, batch).astype(int).tolist()
+    g = torch.Generator(device="cuda").manual_seed(4096)
+    kc, vc = poisoned_caches(g, batch, max_seq, n_kv * hd, positions)
+    q = rn(g, batch, n_heads * hd)
+    scale = float(np.float32(1.0 / math.sqrt(hd)))
+    ref = ref_attention(q, kc, vc, positions, n_heads, n_kv, hd, max_seq, scale)
+    absv = attention_abs_terms(q, kc, vc, positions, n_heads, n_kv, hd, scale)
+    kh, vh = head_major(kc, n_kv, hd), head_major(vc, n_kv, hd)
+    for rep in range(2):
+        out = split_attention(q, kh, vh, positions, n_heads, n_kv, hd, max_seq, scale)
+        check_close(out, ref, absv, f"config-4 split attention B=32 pos 3900..4200 rep {rep}")
+    assert q3.device_error() == 0
+
+
+def test_attention_batch1_at_position_8191():
+    """Config 3's last position through both batch-1 attention paths."""
+    n_heads, n_kv, hd, max_seq, p = 32, 8, 128, 8192, 8191
+    kvd = n_kv * hd
+    g = torch.Generator(device="cuda").manual_seed(8191)
+    kc, vc = poisoned_caches(g, 1, max_seq, kvd, [p])
+    q, k, v = rn(g, 1, n_heads * hd), rn(g, 1, kvd), rn(g, 1, kvd)
+    qn, kn = rn(g, hd, std=0.02, mean=1.0), rn(g, hd, std=0.02, mean=1.0)
+    pos = torch.tensor([p], dtype=torch.int32, device="cuda")
+    scale = float(np.float32(1.0 / math.sqrt(hd)))
+    # the reference: qk_norm_rope (writes row p of the caches), then attention
+    rq, rk, rkc, rvc = q.clone(), k.clone(), kc.clone(), vc.clone()
+    ref_kernels.call("qk_norm_rope_forward", rq.data_ptr(), rk.data_ptr(), v.data_ptr(), qn.data_ptr(), kn.data_ptr(),
+                     rkc.data_ptr(), rvc.data_ptr(), pos.data_ptr(), n_heads, n_kv, hd, EPS, THETA, None, None,
+                     stream())
+    ref = ref_attention(rq, rkc, rvc, [p], n_heads, n_kv, hd, max_seq, scale)
+    absv = attention_abs_terms(rq, rkc, rvc, [p], n_heads, n_kv, hd, scale)
+
+    # split path on the reference's roped q and caches
+    out = split_attention(rq, head_major(rkc, n_kv, hd), head_major(rvc, n_kv, hd), [p], n_heads, n_kv, hd, max_seq,
+                          scale)
+    check_close(out, ref, absv, "split attention B=1 pos 8191")
+
+    # fused RoPE + attention from the raw projections, the engine's batch-1 path
+    chunks = _lib.load().q3_rope_attention_chunks(1, n_heads, n_kv, hd, max_seq)
+    assert chunks >= 2
+    kh, vh = head_major(kc, n_kv, hd), head_major(vc, n_kv, hd)
+    out = torch.full_like(q, float("nan"))
+    _lib.call("q3_rope_attention_batched", out.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(), qn.data_ptr(),
+              kn.data_ptr(), kh.data_ptr(), vh.data_ptr(), n_kv * max_seq * hd, hd, max_seq * hd, pos.data_ptr(), 1,
+              n_heads, n_kv, hd, max_seq, EPS, THETA, scale, chunks, stream())
+    torch.cuda.synchronize()
+    check_equal(kh[0, :, p], head_major(rkc, n_kv, hd)[0, :, p], "fused attention: key row 8191")
+    check_equal(vh[0, :, p], head_major(rvc, n_kv, hd)[0, :, p], "fused attention: value row 8191")
+    check_close(out, ref, absv, f"fused attention B=1 pos 8191 ({chunks} chunks)")
+    assert q3.device_error() == 0
+
+
+def test_engine_batch32_qwen3_4b_slice_matches_reference():
+    """The benchmark's engine (Qwen3-4B shapes, 32 sequences, KV 4096) on a 2-layer cut, 16 steps."""
+    full = checkpoint.PRESETS["qwen3-4b"]
+    shape = checkpoint.Qwen3Shape(full.hidden_size, full.intermediate_size, 2, full.num_attention_heads,
+                                  full.num_key_value_heads, full.head_dim, full.vocab_size)
+    B, prefill, steps = 32, 4096, 16
+    max_seq = prefill + steps + 8
+    n_kv, hd, L = shape.num_key_value_heads, shape.head_dim, shape.num_hidden_layers
+    w = DeviceWeights.random(shape, seed=3)
+    eng = Engine(w, batch=B, max_seq=max_seq)
+    eng.fill_kv_normal(prefill, seed=17)
+    eng.synchronize()
+    # the engine's caches are [layer][B][n_kv][max_seq][hd]; each reference sequence gets its own
+    # [layer][max_seq][n_kv*hd] copy of the same values
+    kcache = q3.engine.device_view(eng.info.key_cache, (L, B, n_kv, max_seq, hd), "bf16")
+    vcache = q3.engine.device_view(eng.info.value_cache, (L, B, n_kv, max_seq, hd), "bf16")
+    sys.path.insert(0, str(HERE.parent / "oracle"))
+    from ref_forward import RefForward
+    refs = []
+    for b in range(B):
+        r = RefForward(w, max_seq)
+        r.kc.copy_(kcache[:, b].permute(0, 2, 1, 3).reshape(L, max_seq, n_kv * hd))
+        r.vc.copy_(vcache[:, b].permute(0, 2, 1, 3).reshape(L, max_seq, n_kv * hd))
+        refs.append(r)
+    torch.cuda.synchronize()
+    rng = np.random.default_rng(7)
+    tokens = rng.integers(0, shape.vocab_size, B).tolist()
+    flips_close, checked, worst_ulp = 0, 0, 0
+    for i in range(steps):
+        pos = prefill + i
+        eng.forward(tokens, [pos] * B)
+        mine_tok = eng.sample_argmax()
+        mine_logits = eng.logits().clone()
+        ref_logits = torch.empty_like(mine_logits)
+        ref_tok = []
+        for b in range(B):
+            ref_logits[b].copy_(refs[b].forward(tokens[b], pos))
+            ref_tok.append(refs[b].argmax())
+        torch.cuda.synchronize()
+        for b in range(B):
+            f = np.sort(O.bf16_to_f32(bits(ref_logits[b])))[::-1]
+            gap = float(f[0] - f[1])
+            if mine_tok[b] != ref_tok[b]:
+                assert gap <= 1e-2, f"step {i} sequence {b}: token {mine_tok[b]} vs reference {ref_tok[b]}, gap {gap:.4f}"
+                flips_close += 1
+            checked += 1
+        # logits: the engine's inputs to the LM head differ from the reference's by what the two
+        # layers' reordered sums left in the residual stream, so the bar here is looser than a
+        # single kernel's: at most 1 ulp for all but 2 % of the logits, every logit within
+        # 2^-5 |ref| + 2^-8 (a few ulps). The figures are recorded for every step.
+        m = O.bf16_to_f32(bits(mine_logits)).reshape(-1)
+        r = O.bf16_to_f32(bits(ref_logits)).reshape(-1)
+        d = O.ulp_diff(bits(mine_logits).reshape(-1), bits(ref_logits).reshape(-1))
+        rec = record(f"4B-slice engine logits step {i}", d, d.size, "<= 1 ulp on >= 98 %, all within 2^-5|ref| + 2^-8")
+        assert rec["over_1ulp"] <= 0.02 * d.size, f"step {i}: {rec['over_1ulp']} logits more than 1 ulp away"
+        excess = np.abs(m - r) - (np.abs(r) * 2.0 ** -5 + 2.0 ** -8)
+        assert excess.max() <= 0, f"step {i}: logit {int(excess.argmax())} mine {m[excess.argmax()]} ref {r[excess.argmax()]}"
+        worst_ulp = max(worst_ulp, rec["max_ulp"])
+        tokens = ref_tok  # teacher forcing: both continue from the reference's tokens
+    record(f"4B-slice engine tokens: {checked} compared, {flips_close} flips at gap <= 1e-2",
+           np.array([flips_close]), checked, "identical where gap > 1e-2")
+    eng.close()
+    assert q3.device_error() == 0

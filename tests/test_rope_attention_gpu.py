@@ -6,8 +6,8 @@ by the drop-in attention_forward (bit-identical to the reference's attention) pe
     or in q, k, v;
   - with one chunk the output is the reference's bit for bit;
   - with the chunk count that fills the GPU, only the fp32 order of the P.V sum differs: the
-    split-attention tolerance of test_batched_gpu.py applies (at most 1 bf16 ulp for all but
-    0.5 % of elements, every element within 2^-7 |ref| + 2^-17 sum |p v|);
+    split-attention bar of tests/parity.check_close applies (at most 1 bf16 ulp for all but
+    0.5 % of elements, every element within 2^-7 |ref| + 2^-17 sum_t p_t |v_t|);
   - every case runs twice, and cache rows past each position hold NaN, which must never be read.
 """
 import math
@@ -27,7 +27,8 @@ pytestmark = pytest.mark.gpu
 
 import llm_inference_b200 as q3  # noqa: E402
 from llm_inference_b200 import _lib  # noqa: E402
-from test_batched_gpu import cache_strides, check_close, rn, stream, to_layout  # noqa: E402
+from parity import attention_abs_terms, check_close  # noqa: E402
+from test_batched_gpu import cache_strides, rn, stream, to_layout  # noqa: E402
 
 EPS, THETA = 1e-6, 1e6
 
@@ -43,7 +44,7 @@ def reference(q, k, v, qn, kn, kc, vc, pos, n_heads, n_kv, hd, max_seq, scale):
     att = torch.empty(n_heads * max_seq, dtype=torch.float32, device="cuda")
     for b in range(batch):
         q3.attention_forward(out[b], q2[b], kc2[b], vc2[b], att, n_heads, n_kv, hd, pos[b:b + 1], max_seq, scale)
-    return kc2, vc2, out
+    return kc2, vc2, out, q2
 
 
 CASES = [  # batch, n_heads, n_kv, hd, positions
@@ -77,7 +78,8 @@ def test_rope_attention_matches_exact_kernels(batch, n_heads, n_kv, hd, position
     qn, kn = rn(g, hd, std=0.02, mean=1.0), rn(g, hd, std=0.02, mean=1.0)
     pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
     scale = float(np.float32(1.0 / math.sqrt(hd)))
-    ref_kc, ref_vc, ref_out = reference(q, k, v, qn, kn, kc, vc, pos, n_heads, n_kv, hd, max_seq, scale)
+    ref_kc, ref_vc, ref_out, q_rope = reference(q, k, v, qn, kn, kc, vc, pos, n_heads, n_kv, hd, max_seq, scale)
+    absv = attention_abs_terms(q_rope, ref_kc, ref_vc, positions, n_heads, n_kv, hd, scale)
     strides = cache_strides(layout, max_seq, n_kv, hd)
     q0, k0, v0 = q.clone(), k.clone(), v.clone()
     # one chunk holds every position's scores in shared memory: too many at 8 query heads per kv
@@ -106,7 +108,7 @@ def test_rope_attention_matches_exact_kernels(batch, n_heads, n_kv, hd, position
             if chunks == 1:
                 assert torch.equal(out.view(torch.int16), ref_out.view(torch.int16)), what
             else:
-                check_close(out, ref_out, np.full(out.numel(), 8.0, np.float32), what)
+                check_close(out, ref_out, absv, f"fused attention B={batch} {n_heads}/{n_kv} hd{hd} {layout} {what}")
 
 
 def test_rope_attention_rejects_bad_arguments():

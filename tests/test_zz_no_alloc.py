@@ -5,9 +5,8 @@ of its GPU memory in one pool at start-up, a plugin running inside another frame
 manager, or a serving loop where an allocation could block or fail in the middle of a request.
 For them q3_attention_batched_static takes its scratch from a fixed array inside the library
 instead of a caller buffer. These tests call it through the C ABI and compare it with
-q3_attention_batched (given a scratch buffer allocated here, in the test) on the same inputs,
-with the tolerance of the batched tests (test_batched_gpu.check_close: at most 1 bf16 ulp for
-all but 0.5 % of elements, every element within the fp32-reordering bound). Two calls in a row
+q3_attention_batched (given a scratch buffer allocated here, in the test) on the same inputs.
+Both run the same deterministic kernels, so the outputs must be bit-identical. Two calls in a row
 use different positions and queries, so the second one runs over what the first left in the
 shared array. A shape that needs more scratch than the array holds must be refused.
 
@@ -30,7 +29,8 @@ pytestmark = pytest.mark.gpu
 
 import llm_inference_b200 as q3  # noqa: E402
 from llm_inference_b200 import _lib  # noqa: E402
-from test_batched_gpu import check_close, rn, stream  # noqa: E402
+from parity import check_equal  # noqa: E402
+from test_batched_gpu import rn, stream  # noqa: E402
 
 STATIC_SCRATCH_BYTES = 32 << 20  # Q3_ATTENTION_STATIC_SCRATCH_BYTES
 Q3_ERR_SCRATCH_LIMIT = 6
@@ -73,7 +73,7 @@ def test_static_scratch_matches_caller_scratch_on_two_calls():
         q = rn(g, 4, n_heads * hd)
         pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
         out, ref = run_both(q, kc, vc, pos, n_heads, n_kv, hd, max_seq)
-        check_close(out, ref, np.full(out.numel(), 8.0, np.float32), f"static scratch, positions {positions}")
+        check_equal(out, ref, f"static scratch, positions {positions}")
     assert q3.device_error() == 0
 
 
