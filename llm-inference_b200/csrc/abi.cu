@@ -32,7 +32,7 @@ unsigned take_error_gemv();
 unsigned take_error_decode();
 unsigned take_error_attention();
 unsigned take_error_tc();
-unsigned take_error_megakernel();
+unsigned take_error_stream();
 unsigned take_error_attn_fused();
 unsigned take_error_selftest();
 
@@ -139,7 +139,7 @@ int q3_device_error(void *stream, unsigned *flags) {
     cudaError_t e = cudaStreamSynchronize(S(stream));
     if (e != cudaSuccess) return q3::record_cuda_error(e);
     *flags = q3::take_error_gemv() | q3::take_error_decode() | q3::take_error_attention() | q3::take_error_tc() |
-             q3::take_error_megakernel() | q3::take_error_attn_fused() | q3::take_error_selftest();
+             q3::take_error_stream() | q3::take_error_attn_fused() | q3::take_error_selftest();
     return Q3_OK;
 }
 

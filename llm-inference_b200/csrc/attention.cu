@@ -25,13 +25,10 @@
 // bit-identical. Split mode (the batched engine): chunks of 512 positions for parallelism; their
 // partial sums are added in chunk order, which changes only fp32 rounding inside the sum.
 //
-// Split mode also moves the dot products onto the tensor cores (attn_scores_tc_kernel):
-// D[128 positions x 16] = K_tile[128 x head_dim] . Q^T, with the K tile and the group's query
-// rows loaded by TMA (128-byte swizzle), one tcgen05.mma per 16 head dims into a double-buffered
-// TMEM accumulator, and the same score rounding in the epilogue. The tensor core sums a dot in
-// its own order, so a score can differ from the serial sum's rounding in rare cases. Its P.V
-// (attn_pv_vec_kernel) gives each thread two adjacent dims (bf16x2 loads) of one half of the
-// positions, all query heads of the group at once (one vector load of their probabilities).
+// Split mode streams the K tiles by TMA into a deep shared-memory ring (attn_scores_exact_kernel)
+// and keeps the reference's serial dot products, so its scores -- and so its probabilities --
+// are the reference's bit for bit; P.V runs on the tensor cores (attn_pv_tc_kernel), where the
+// products p * v are exact and only the fp32 order of the sums differs.
 #include <math.h>
 
 #include <algorithm>
@@ -496,139 +493,199 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
     }
 }
 
-// ------------------------------------------------------------------ scores on tcgen05 (split mode)
-constexpr int TC_TILE = 128;        // positions per item = MMA M
-constexpr int TC_N = 16;            // MMA N: query heads of the group, padded
-#ifndef Q3_SCORES_STAGES
-#define Q3_SCORES_STAGES 4
-#endif
-constexpr int TC_STAGES = Q3_SCORES_STAGES;
-constexpr int TC_ACC = 4;           // TMEM accumulators (TC_N columns each)
-constexpr int TC_THREADS = 192;     // producer warp, MMA warp, 4 epilogue warps
+// ------------------------------------------------------------------ scores, TMA-fed (split mode)
+// The reference's score arithmetic, bit for bit, at streaming speed. One item = (b, kv head, 128
+// positions). A producer thread loads the item's K tile by TMA as head_dim / 64 boxes of
+// [128 positions][64 dims] (128-byte swizzle), one box per ring stage, into a ring of SX_STAGES
+// boxes, never waiting for anything but a free stage, so the cache streams while the dot products
+// run. Four groups of two consumer warps take the CTA's items in turn; in a group, thread r owns
+// the positions r and r + 64 of the tile. For each box it copies its two rows' 128-byte pieces
+// into registers and frees the stage at once -- the ring then holds almost only copies in
+// flight, which is what keeps HBM busy -- and then computes, for each of its two rows and every
+// query head of the kv group, the reference's dot product: one fp32 chain per (row, head), dims
+// in order, one fused multiply-add each (src/kernels.cu:455-460, where nvcc fuses
+// `dot += q * k`), then s = round_bf16(round_bf16(dot) * scale). The group's query heads sit in
+// shared memory as fp32 [dim][head], so one vector load gives a dim's value for every head and
+// serves both rows. The swizzle puts the 16-byte chunk c of row r at chunk c ^ (r % 8): a warp's
+// 32 threads reading the same logical chunk of 32 consecutive rows need only the four wavefronts
+// of their 512 bytes.
+constexpr int SX_TILE = 128;
+constexpr int SX_BOX = SX_TILE * 128;  // one 64-dim box: 16 KB
+constexpr int SX_STAGES = 12;
+constexpr int SX_GROUPS = 4;
+constexpr int SX_GWARPS = 2;                    // warps per group: 64 threads, two rows each
+constexpr int SX_THREADS = 32 + SX_GROUPS * SX_GWARPS * 32;  // producer warp + the consumer groups
 
-struct ScoreTcPlan {
-    int halves;         // head_dim / 64
-    int k_rows_per_seq; // rows of the K map per sequence (kv.seq / kv.pos)
+struct ScoreXPlan {
+    int halves;           // head_dim / 64: boxes per item
+    int k_rows_per_seq;   // rows of the K map per sequence (kv.seq / kv.pos)
     int k_rows_per_head;  // head-major caches: rows per kv head (kv.head / kv.pos), else 0
     int k_cols_per_head;  // heads within a row: columns per kv head (kv.head), else 0
-    int stage_bytes;
-    uint32_t idesc;
 };
 
+__device__ __forceinline__ void group_sync(int group) {
+    asm volatile("bar.sync %0, %1;" ::"r"(1 + group), "n"(SX_GWARPS * 32) : "memory");
+}
+
+// True in every thread of the group if `v` is true in any (a barrier of the group).
+__device__ __forceinline__ bool group_any(int group, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(1 + group), "n"(SX_GWARPS * 32)
+        : "memory");
+    return r != 0;
+}
+
+// q values of one dim for the NREP heads: one shared-memory vector load
 template <int NREP>
-__global__ void __launch_bounds__(TC_THREADS, 1)
-    attn_scores_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                          const __grid_constant__ AttnArgs a, const __grid_constant__ ScoreTcPlan pl) {
+struct QVec {
+    float v[NREP];
+};
+template <int NREP>
+__device__ __forceinline__ QVec<NREP> load_q(const float *p) {
+    QVec<NREP> q;
+    if constexpr (NREP % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NREP; i += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(p + i);
+            q.v[i] = f.x;
+            q.v[i + 1] = f.y;
+            q.v[i + 2] = f.z;
+            q.v[i + 3] = f.w;
+        }
+    } else if constexpr (NREP == 2) {
+        const float2 f = *reinterpret_cast<const float2 *>(p);
+        q.v[0] = f.x;
+        q.v[1] = f.y;
+    } else {
+        q.v[0] = p[0];
+    }
+    return q;
+}
+
+template <int NREP>
+__global__ void __launch_bounds__(SX_THREADS, 1)
+    attn_scores_exact_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ AttnArgs a,
+                             const __grid_constant__ ScoreXPlan pl) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    const int kbytes = TC_TILE * 128;  // one 64-dim half of the K tile
-    const int qbytes = TC_N * 128;     // one 64-dim half of the query rows
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)TC_STAGES * pl.stage_bytes);
-    uint64_t *empty = full + TC_STAGES;
-    uint64_t *acc_full = empty + TC_STAGES;    // [TC_ACC]
-    uint64_t *acc_empty = acc_full + TC_ACC;   // [TC_ACC]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + TC_ACC);
-    int *prefix = reinterpret_cast<int *>(tmem_slot + 4);
+    const int hd = a.head_dim;
+    float *q_all = reinterpret_cast<float *>(smem + (size_t)SX_STAGES * SX_BOX);  // [SX_GROUPS][hd][NREP]
+    uint64_t *full = reinterpret_cast<uint64_t *>(q_all + SX_GROUPS * NREP * hd);
+    uint64_t *empty = full + SX_STAGES;
+    int *prefix = reinterpret_cast<int *>(empty + SX_STAGES);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < TC_STAGES; i++) {
+        for (int i = 0; i < SX_STAGES; i++) {
             mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 1);
-        }
-        for (int i = 0; i < TC_ACC; i++) {
-            mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
+            mbar_init(&empty[i], SX_GWARPS);  // the warps of the group that reads the box
         }
         fence_barrier_init();
         prefetch_tmap(&tmK);
-        prefetch_tmap(&tmQ);
     }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TC_ACC * TC_N)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
     __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
-    pdl_wait();  // positions and the newest cache rows come from the previous kernels
-    // prefix table (thread 0 of the CTA builds it; build_prefix synchronizes all threads)
-    const int total = build_prefix(a, TC_TILE, prefix);
+    pdl_wait();  // positions, queries and the newest cache rows come from the previous kernels
+    const int total = build_prefix(a, SX_TILE, prefix);
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     const int n = i1 - i0;
     int cur = n > 0 ? first_seq(prefix, a.B, i0) : 0;  // this thread's sequence cursor
 
-    if (warp == 0 && lane == 0) {
-        // ---------------- producer
-        const uint64_t stream_pol = policy_evict_first();  // K rows are read once per step
-        int k = 0;
-        for (; k < n; k++) {
-            const int st = k % TC_STAGES;
-            if (k >= TC_STAGES && !mbar_wait(&empty[st], ((k / TC_STAGES) - 1) & 1, &g_dev_error)) break;
-            const Item it = item_at(a, prefix, TC_TILE, i0 + k, cur);
-            unsigned char *base = smem + (size_t)st * pl.stage_bytes;
-            mbar_arrive_expect_tx(&full[st], (uint32_t)pl.halves * (kbytes + qbytes));
-            const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * TC_TILE;
-            const int qrow = it.b * a.n_heads + it.kvh * NREP;
-            for (int h = 0; h < pl.halves; h++) {
-                tma_load_2d_stream(base + h * kbytes, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow, &full[st], stream_pol);
-                tma_load_2d(base + pl.halves * kbytes + h * qbytes, &tmQ, h * TMA_BK, qrow, &full[st]);
-            }
-        }
-        for (int j = max(0, k - TC_STAGES); j < k; j++) mbar_wait(&full[j % TC_STAGES], (j / TC_STAGES) & 1, &g_dev_error);
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer: 16 head dims per instruction
-        for (int k = 0; k < n; k++) {
-            const int st = k % TC_STAGES, buf = k % TC_ACC;
-            if (k >= TC_ACC && !mbar_wait(&acc_empty[buf], ((k / TC_ACC) - 1) & 1, &g_dev_error)) break;
-            if (!mbar_wait(&full[st], (k / TC_STAGES) & 1, &g_dev_error)) break;
-            tc_fence_after();
-            const uint32_t kb = smem_u32(smem + (size_t)st * pl.stage_bytes);
-            const uint32_t qb = kb + pl.halves * kbytes;
-            for (int kk = 0; kk < pl.halves * 4; kk++) {
-                const int h = kk >> 2, o = (kk & 3) * 32;
-                mma_bf16(tmem_base + buf * TC_N, smem_desc_sw128(kb + h * kbytes + o), smem_desc_sw128(qb + h * qbytes + o),
-                         pl.idesc, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&empty[st]);
-            mma_commit(&acc_full[buf]);
-        }
-    } else if (warp >= 2) {
-        // ---------------- epilogue: one position per thread
-        const int quarter = warp % 4;
-        const int row = quarter * 32 + lane;
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-        for (int k = 0; k < n; k++) {
-            const int buf = k % TC_ACC;
-            // warp-uniform exit: tcgen05.ld below is warp-collective
-            if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (k / TC_ACC) & 1, &g_dev_error))) break;
-            tc_fence_after();
-            float acc[8];
-            tmem_ld8(lane_addr + buf * TC_N, acc);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-            const Item it = item_at(a, prefix, TC_TILE, i0 + k, cur);
-            const int t = it.c * TC_TILE + row;
-            if (t < it.len) {
-                float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld + t;
-#pragma unroll
-                for (int h = 0; h < NREP; h++) sc[(size_t)h * a.ld] = round_bf16(round_bf16(acc[h]) * a.scale);
-            }
-        }
-    }
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
     if (warp == 0) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TC_ACC * TC_N)
-                     : "memory");
+        if (lane == 0) {
+            // ---------------- producer: box j of the ring is box j % halves of item j / halves
+            const uint64_t stream_pol = policy_evict_first();  // K rows are read once per step
+            const int nbox = n * pl.halves;
+            int j = 0;
+            for (; j < nbox; j++) {
+                const int st = j % SX_STAGES;
+                if (j >= SX_STAGES && !mbar_wait(&empty[st], ((j / SX_STAGES) - 1) & 1, &g_dev_error)) break;
+                const int h = j % pl.halves;
+                const Item it = item_at(a, prefix, SX_TILE, i0 + j / pl.halves, cur);
+                mbar_arrive_expect_tx(&full[st], (uint32_t)SX_BOX);
+                const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * SX_TILE;
+                tma_load_2d_stream(smem + (size_t)st * SX_BOX, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow,
+                                   &full[st], stream_pol);
+            }
+            // copies still in flight land before the CTA exits (bounded waits)
+            for (int i = max(0, j - SX_STAGES); i < j; i++)
+                mbar_wait(&full[i % SX_STAGES], (i / SX_STAGES) & 1, &g_dev_error);
+        }
+        return;
+    }
+    // ---------------- consumers: group g takes items g, g + SX_GROUPS, ...
+    const int group = (warp - 1) / SX_GWARPS;
+    const int gt = threadIdx.x - 32 - group * SX_GWARPS * 32;  // 0..63
+    float *q_s = q_all + group * NREP * hd;                    // [hd][NREP]
+    int qb = -1, qk = -1;
+    const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
+    bool failed = false;
+    for (int k = group; k < n && !failed; k += SX_GROUPS) {
+        const Item it = item_at(a, prefix, SX_TILE, i0 + k, cur);
+        if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
+            group_sync(group);             // nobody still reads the previous ones
+            const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
+            for (int j = gt; j < NREP * hd; j += SX_GWARPS * 32) q_s[(j % hd) * NREP + j / hd] = __bfloat162float(qg[j]);
+            group_sync(group);
+            qb = it.b;
+            qk = it.kvh;
+        }
+        const int ta = it.c * SX_TILE + gt, tb = ta + 64;
+        float acc_a[NREP], acc_b[NREP];
+#pragma unroll
+        for (int h = 0; h < NREP; h++) {
+            acc_a[h] = 0.0f;
+            acc_b[h] = 0.0f;
+        }
+        for (int half = 0; half < pl.halves; half++) {
+            const int j = k * pl.halves + half;  // ring box
+            const int st = j % SX_STAGES;
+            const bool ok = mbar_wait(&full[st], (j / SX_STAGES) & 1, &g_dev_error);
+            // a timed-out wait ends the group's loop in all of its threads together (the group
+            // barriers above need all of them)
+            failed = group_any(group, !ok);
+            bf16x8 ka[8], kb[8];
+            if (ok) {
+                const unsigned char *rowa = smem + (size_t)st * SX_BOX + gt * 128;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    ka[c] = lds128(rowa + ((c ^ sw) << 4));
+                    kb[c] = lds128(rowa + 64 * 128 + ((c ^ sw) << 4));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);  // the rows are in registers: the box is free
+            if (failed) break;
+            const float *qd = q_s + half * 64 * NREP;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const QVec<NREP> q = load_q<NREP>(qd + (c * 8 + e) * NREP);
+                    const float fa = e & 1 ? __high2float(ka[c].h[e / 2]) : __low2float(ka[c].h[e / 2]);
+                    const float fb = e & 1 ? __high2float(kb[c].h[e / 2]) : __low2float(kb[c].h[e / 2]);
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) {
+                        acc_a[h] = __fmaf_rn(q.v[h], fa, acc_a[h]);
+                        acc_b[h] = __fmaf_rn(q.v[h], fb, acc_b[h]);
+                    }
+                }
+            }
+        }
+        if (failed) break;
+        float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
+#pragma unroll
+        for (int h = 0; h < NREP; h++) {
+            if (ta < it.len) sc[(size_t)h * a.ld + ta] = round_bf16(round_bf16(acc_a[h]) * a.scale);
+            if (tb < it.len) sc[(size_t)h * a.ld + tb] = round_bf16(round_bf16(acc_b[h]) * a.scale);
+        }
     }
 }
 
@@ -1036,23 +1093,20 @@ long long cache_map_rows(const AttnArgs &a) {
 }
 
 template <int NREP>
-int launch_scores_tc(const AttnArgs &a, cudaStream_t s) {
-    ScoreTcPlan pl;
+int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
+    ScoreXPlan pl;
     pl.halves = a.head_dim / TMA_BK;
     pl.k_rows_per_seq = (int)(a.kv.seq / a.kv.pos);
     pl.k_rows_per_head = a.kv.head >= a.kv.pos ? (int)(a.kv.head / a.kv.pos) : 0;
     pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
-    pl.stage_bytes = pl.halves * (TC_TILE * 128 + TC_N * 128);
-    // kind::f16: fp32 accumulate, bf16 A and B, both K-major, N = 16, M = 128
-    pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) | ((uint32_t)(TC_TILE >> 4) << 24);
-    CUtensorMap mk, mq;
-    if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, TC_TILE)) return Q3_ERR_ARG;
-    if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TC_N)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)TC_STAGES * pl.stage_bytes + 256 + (size_t)PREFIX_INTS(a.B) * 4;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_tc_kernel<NREP>), smem));
-    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + TC_TILE - 1) / TC_TILE);
+    CUtensorMap mk;
+    if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, SX_TILE)) return Q3_ERR_ARG;
+    const size_t smem = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)SX_GROUPS * NREP * a.head_dim * 4 +
+                        2 * SX_STAGES * 8 + (size_t)PREFIX_INTS(a.B) * 4;
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_exact_kernel<NREP>), smem));
+    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + SX_TILE - 1) / SX_TILE);
     const int grid = (int)std::min<long long>(max_items, num_sms());
-    Q3_TRY_LAUNCH(launch(attn_scores_tc_kernel<NREP>, dim3(grid), dim3(TC_THREADS), smem, s, 1, mk, mq, a, pl));
+    Q3_TRY_LAUNCH(launch(attn_scores_exact_kernel<NREP>, dim3(grid), dim3(SX_THREADS), smem, s, 1, mk, a, pl));
     return Q3_OK;
 }
 
@@ -1099,7 +1153,7 @@ int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     const bool split = a.stats != nullptr;
     const size_t prefix_bytes = (size_t)PREFIX_INTS(a.B) * 4;
     if (split && split_fast_path(a)) {
-        int st = launch_scores_tc<NREP>(a, s);
+        int st = launch_scores_exact<NREP>(a, s);
         if (st != Q3_OK) return st;
         st = launch_stats<NREP>(a, s);
         if (st != Q3_OK) return st;

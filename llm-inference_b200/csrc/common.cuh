@@ -196,37 +196,44 @@ struct KvLayout {
     long long seq, pos, head;
 };
 
-// Scratch of the split-KV attention (attention.cu): softmax statistics and per-chunk partial
-// outputs (the counters are unused).
-// Batch-1 persistent decode kernel (megakernel.cu): per-layer weight pointers and the step's
-// buffers, filled by the engine.
+// Batch-1 decode step as one persistent kernel (decode_stream.cu): per-layer weight pointers
+// and the step's buffers, filled by the engine.
 struct MkLayer {
     const bf16 *attn_norm, *wq, *wk, *wv, *q_norm, *k_norm, *wo, *mlp_norm, *w_gate, *w_up, *w_down;
 };
 
-struct MkParams {
+constexpr int DS_STAGE_BYTES = 40960;  // one stage of the weight ring: whole rows, 8 of 5 KB, 2 of 19 KB
+constexpr int DS_MAX_STAGES = 8;
+
+struct DsParams {
     const MkLayer *layers;  // device array [n_layers]
     const bf16 *embed, *final_norm, *lm_head;
-    int n_layers, H, I, n_heads, n_kv, hd, vocab;
+    int n_layers, H, I, n_heads, n_kv, vocab;  // head_dim is 128
     float eps, theta, scale;
     bf16 *x, *q, *k, *v, *attn_out, *act, *logits;
-    bf16 *key_cache, *value_cache;  // layer l at + l * layer_stride; [n_kv][max_seq][hd]
+    bf16 *key_cache, *value_cache;  // layer l at + l * layer_stride; [n_kv][max_seq][128]
     long long layer_stride;
     int max_seq;
     float *scores;   // [n_heads][ld]
     int ld;
-    float *stats;    // [n_heads][2]
-    float *partial;  // [2 * max_items][n_heads][hd]
-    float *amax_val;  // [gridDim.x]
+    float *cmax;     // [n_kv][chunks][n_heads / n_kv] chunk maxima
+    float *csum;     // [n_kv][n_heads / n_kv * 128] softmax sum chains
+    float *partial;  // [n_kv][chunks][n_heads / n_kv][128] P.V partial sums
+    float *amax_val;  // [grid]
     int *amax_idx;
+    unsigned *sync;  // barrier counters and the error word (decode_stream_sync_words), zero at rest
     int *next_token, *pos, *out_token, *history, *step;
     int history_cap;
-    unsigned *bar;   // [0] arrivals, [1] generation, [2] error (sticky)
+    int stages;      // weight-ring depth (decode_stream_plan)
+    int chunks;      // attention CTAs per kv head (decode_stream_plan)
 };
 
-int megakernel_grid(int nrep);
-int megakernel_launch(const MkParams &p, int nrep, int grid, cudaStream_t s);
+int decode_stream_plan(DsParams &p);  // grid (one CTA per SM), or 0 if the shapes do not fit
+int decode_stream_launch(const DsParams &p, int grid, cudaStream_t s);
+int decode_stream_sync_words(int n_kv);
 
+// Scratch of the split-KV attention (attention.cu): softmax statistics and per-chunk partial
+// outputs (the counters are unused).
 struct AttnSplit {
     float *stats;
     float *partial;

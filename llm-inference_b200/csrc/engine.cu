@@ -84,10 +84,11 @@ struct q3_engine {
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
     int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
-    // Q3_ENGINE_MEGAKERNEL: the whole step as one cooperative kernel (batch 1)
+    // Q3_ENGINE_MEGAKERNEL: the whole step as one persistent kernel with a streamed weight ring
+    // (decode_stream.cu, batch 1)
     bool mk = false;
-    MkParams mkp = {};
-    int mk_nrep = 0, mk_grid = 0;
+    DsParams mkp = {};
+    int mk_grid = 0;
     int *host_io;  // pinned: [2B] for token/position uploads, [B] for downloads
     cudaGraphExec_t graph;
     int graph_kernels;  // kernel nodes of the captured step
@@ -174,7 +175,7 @@ int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int c
 }
 
 int enqueue_step(q3_engine *e) {
-    if (e->mk) return megakernel_launch(e->mkp, e->mk_nrep, e->mk_grid, e->stream);
+    if (e->mk) return decode_stream_launch(e->mkp, e->mk_grid, e->stream);
     const q3_config &c = e->cfg;
     const int B = e->B;
     cudaStream_t s = e->stream;
@@ -223,9 +224,7 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     st = attention_check(c.n_heads, c.n_kv_heads, c.head_dim, max_seq, batch);
     if (st != Q3_OK) return st;
     const bool mk = (flags & Q3_ENGINE_MEGAKERNEL) != 0;
-    if (mk && (batch != 1 || (c.head_dim != 64 && c.head_dim != 128) || c.hidden_size > 8192 ||
-               ((long long)c.n_heads * c.head_dim) % 8))
-        return Q3_ERR_SHAPE;
+    if (mk && (batch != 1 || c.head_dim != 128)) return Q3_ERR_SHAPE;
     q3_engine *e = new q3_engine();
     e->cfg = c;
     e->layers.assign(w->layers, w->layers + c.n_layers);
@@ -276,15 +275,23 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
         e->fused_chunks = fused_chunks(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq);
     if (mk) {
         e->mk = true;
-        e->mk_nrep = c.n_heads / c.n_kv_heads;
-        e->mk_grid = megakernel_grid(e->mk_nrep);
-        if (e->mk_grid <= 0 && r == Q3_OK) r = Q3_ERR_DEVICE;
-        const size_t parts = (size_t)((max_seq + 255) / 256) * (256 / c.head_dim);
-        A((void **)&e->mkp.partial, parts * qd * 4);
-        A((void **)&e->mkp.amax_val, (size_t)std::max(e->mk_grid, 1) * 4);
-        A((void **)&e->mkp.amax_idx, (size_t)std::max(e->mk_grid, 1) * 4);
-        A((void **)&e->mkp.bar, 16);
-        A((void **)&e->mkp.layers, (size_t)c.n_layers * sizeof(MkLayer));
+        DsParams &p = e->mkp;
+        p.n_layers = c.n_layers;
+        p.H = c.hidden_size;
+        p.I = c.intermediate_size;
+        p.n_heads = c.n_heads;
+        p.n_kv = c.n_kv_heads;
+        p.vocab = c.vocab_size;
+        e->mk_grid = decode_stream_plan(p);
+        if (e->mk_grid <= 0 && r == Q3_OK) r = Q3_ERR_SHAPE;
+        const size_t nrep = (size_t)c.n_heads / c.n_kv_heads, groups = (size_t)c.n_kv_heads * std::max(p.chunks, 1);
+        A((void **)&p.cmax, groups * nrep * 4);
+        A((void **)&p.csum, (size_t)c.n_kv_heads * nrep * 128 * 4);
+        A((void **)&p.partial, groups * nrep * 128 * 4);
+        A((void **)&p.amax_val, (size_t)std::max(e->mk_grid, 1) * 4);
+        A((void **)&p.amax_idx, (size_t)std::max(e->mk_grid, 1) * 4);
+        A((void **)&p.sync, (size_t)decode_stream_sync_words(c.n_kv_heads) * 4);
+        A((void **)&p.layers, (size_t)c.n_layers * sizeof(MkLayer));
     }
     if (r == Q3_OK) r = record_cuda_error(cudaMallocHost((void **)&e->host_io, 3 * B * sizeof(int)));
     if (r != Q3_OK) {
@@ -310,19 +317,14 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
         }
         r = record_cuda_error(cudaMemcpyAsync((void *)e->mkp.layers, lw.data(), lw.size() * sizeof(MkLayer),
                                               cudaMemcpyHostToDevice, s));
-        if (r == Q3_OK) r = record_cuda_error(cudaMemsetAsync(e->mkp.bar, 0, 16, s));
+        if (r == Q3_OK)
+            r = record_cuda_error(
+                cudaMemsetAsync(e->mkp.sync, 0, (size_t)decode_stream_sync_words(c.n_kv_heads) * 4, s));
         if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(s));  // `lw` leaves scope
-        MkParams &p = e->mkp;
+        DsParams &p = e->mkp;
         p.embed = e->embed;
         p.final_norm = e->final_norm;
         p.lm_head = e->lm_head;
-        p.n_layers = c.n_layers;
-        p.H = c.hidden_size;
-        p.I = c.intermediate_size;
-        p.n_heads = c.n_heads;
-        p.n_kv = c.n_kv_heads;
-        p.hd = c.head_dim;
-        p.vocab = c.vocab_size;
         p.eps = c.rms_norm_eps;
         p.theta = c.rope_theta;
         p.scale = (float)(1.0 / sqrt((double)c.head_dim));
@@ -339,7 +341,6 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
         p.max_seq = max_seq;
         p.scores = e->scores;
         p.ld = score_ld(max_seq);
-        p.stats = e->split.stats;
         p.next_token = e->next_token;
         p.pos = e->pos;
         p.out_token = e->out_token;
