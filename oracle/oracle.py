@@ -49,6 +49,7 @@ def lib():
             "oracle_gate_up": [P, P, P, P, I, I, P, P],
             "oracle_qk_norm_rope": [P, P, P, P, P, P, P, I, I, I, I, F, F, P, P],
             "oracle_attention": [P, P, P, P, I, I, I, I, F],
+            "oracle_scores": [P, P, P, I, I, I, I, F],
             "oracle_argmax": [P, I],
             "oracle_sample": [P, I, F, F],
         }
@@ -167,6 +168,14 @@ def attention(q, key_cache, value_cache, n_heads, n_kv_heads, head_dim, pos, sca
     out = np.empty(n_heads * head_dim, np.uint16)
     lib().oracle_attention(_p(out), _p(np.ascontiguousarray(q)), _p(key_cache), _p(value_cache),
                            n_heads, n_kv_heads, head_dim, int(pos), float(scale))
+    return out
+
+
+def scores(q, key_cache, n_heads, n_kv_heads, head_dim, pos, scale):
+    """[n_heads][pos + 1] float32 attention scores, the reference's rounding (src/kernels.cu:450-461)."""
+    out = np.empty((n_heads, pos + 1), np.float32)
+    lib().oracle_scores(_p(out), _p(np.ascontiguousarray(q)), _p(np.ascontiguousarray(key_cache)), n_heads,
+                        n_kv_heads, head_dim, int(pos), float(scale))
     return out
 
 

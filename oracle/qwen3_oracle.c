@@ -218,6 +218,23 @@ void oracle_qk_norm_rope(bf16_t *q, bf16_t *k, const bf16_t *v, const bf16_t *q_
     free(normed);
 }
 
+/* The scores step of src/kernels.cu:450-461 alone: scores[h][t] = round_bf16(round_bf16(dot) * scale)
+ * with dot the serial fused multiply-add chain over head_dim, for t = 0..pos, into out[h * (pos + 1) + t]. */
+void oracle_scores(float *out, const bf16_t *q, const bf16_t *key_cache, int n_heads, int n_kv_heads, int head_dim,
+                   int pos, float scale) {
+    int n_rep = n_heads / n_kv_heads;
+    int kv_dim = n_kv_heads * head_dim;
+    for (int h = 0; h < n_heads; h++) {
+        const bf16_t *qh = q + (size_t)h * head_dim;
+        for (int t = 0; t <= pos; t++) {
+            const bf16_t *kt = key_cache + (size_t)t * kv_dim + (size_t)(h / n_rep) * head_dim;
+            float dot = 0.0f;
+            for (int d = 0; d < head_dim; d++) dot = fmaf(bf2f(qh[d]), bf2f(kt[d]), dot);
+            out[(size_t)h * (pos + 1) + t] = round_bf16(round_bf16(dot) * scale);
+        }
+    }
+}
+
 /* src/kernels.cu:439-497 attention_kernel, 128 threads per q head (:492).
  * block_sum (:406-420): xor tree per warp, then a serial sum of the warp partials. */
 void oracle_attention(bf16_t *out, const bf16_t *q, const bf16_t *key_cache,

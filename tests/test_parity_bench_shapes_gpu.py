@@ -269,3 +269,45 @@ def test_engine_batch1_qwen3_4b_slice_to_position_8191(path):
         token = ref_tok
     eng.close()
     assert q3.device_error() == 0
+
+
+@pytest.mark.parametrize("case", ["config4", "edges", "large"])
+def test_split_scores_bit_identical_to_serial_dot(case):
+    """The split path's scores (scratch offset 0, [B][n_heads][ld] fp32) against the CPU oracle's
+    serial fused multiply-add chain (the reference's scores), every valid (sequence, head,
+    position) bit for bit. At head_dim 128 they come from the tensor cores with the exact
+    recomputation of every dot that lies near a bf16 rounding boundary; "large" scales K so that
+    the products and their bound grow, "edges" has positions 0, 1, 127, 128 and 255."""
+    n_heads, n_kv, hd = 32, 8, 128
+    if case == "config4":
+        positions, max_seq, kscale = np.linspace(3900, 4200, 6).astype(int).tolist(), 4224, 1.0
+    elif case == "edges":
+        positions, max_seq, kscale = [0, 1, 127, 128, 255], 256, 1.0
+    else:
+        positions, max_seq, kscale = [1000, 2047], 2048, 40.0
+    batch = len(positions)
+    g = torch.Generator(device="cuda").manual_seed(len(case))
+    kc = (rn(g, batch, max_seq, n_kv * hd).float() * kscale).bfloat16()
+    vc = rn(g, batch, max_seq, n_kv * hd)
+    q = rn(g, batch, n_heads * hd)
+    scale = float(np.float32(1.0 / math.sqrt(hd)))
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    nbytes = _lib.load().q3_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq)
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    out = torch.empty_like(q)
+    kh, vh = head_major(kc, n_kv, hd), head_major(vc, n_kv, hd)
+    _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), kh.data_ptr(), vh.data_ptr(), n_kv * max_seq * hd, hd,
+              max_seq * hd, scratch.data_ptr(), pos.data_ptr(), batch, n_heads, n_kv, hd, max_seq, scale, stream())
+    torch.cuda.synchronize()
+    ld = (max_seq + 3) // 4 * 4
+    sc = scratch[:batch * n_heads * ld * 4].view(torch.float32).view(batch, n_heads, ld).cpu().numpy()
+    kcpu, qcpu = bits(kc), bits(q)
+    mismatches = 0
+    for b, p in enumerate(positions):
+        ref = O.scores(qcpu[b], kcpu[b, :p + 1], n_heads, n_kv, hd, p, scale)
+        mine = sc[b, :, :p + 1]
+        mismatches += int(np.count_nonzero(mine.view(np.uint32) != ref.view(np.uint32)))
+    record(f"split-path scores vs serial dot, {case} ({batch} sequences)", np.array([mismatches]),
+           sum(p + 1 for p in positions) * n_heads, "bit-identical")
+    assert mismatches == 0, f"{mismatches} scores differ from the serial dot"
+    assert q3.device_error() == 0
