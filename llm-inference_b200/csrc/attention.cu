@@ -689,248 +689,6 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     }
 }
 
-// ------------------------------------------------------------------ scores, tensor cores + exact fixups
-// The tensor-core dot products, made exact. For head_dim 128 this kernel replaces
-// attn_scores_exact_kernel: it streams the K tile [128 positions][128 dims] and the group's query
-// rows by TMA (128-byte swizzle) and computes D1 = K . Q^T with tcgen05 (fp32 accumulation in the
-// tensor core's own order), and, from copies of both tiles with the sign bits cleared, D2 =
-// |K| . |Q|^T, the sum of the absolute products of every dot. The reference's serial fp32 chain
-// differs from the exact dot by at most 128 u * sum|p| = 2^-17 * sum|p| (u = 2^-24); the tensor
-// core's sum by at most about 2^-16 * sum|p| even if it truncated every product to the largest
-// one's exponent in each 16-product step. So with E = 2^-14 * D2 (margin over both), every value
-// the serial chain can produce lies in [D1 - E, D1 + E]. When both ends of that interval round to
-// the same bf16 value (ends taken with directed rounding), round_bf16(serial dot) is that value,
-// and the score round_bf16(round_bf16(dot) * scale) follows. Otherwise the (position, head) goes
-// on a list, and the epilogue threads recompute the listed dots exactly as the reference does --
-// one fp32 fused multiply-add per dim, in order (src/kernels.cu:455-460) -- from the K row and
-// query row still in shared memory. Every score is the reference's bit for bit.
-//
-//   warp 0        TMA producer: K tile + query rows per stage, into a TH_STAGES ring
-//   warp 1        MMA issuer: D1 when a stage lands, D2 when its sign-stripped copy is ready
-//   warps 2-5     epilogue: one position per thread, the interval test, the listed fixups
-//   warps 6-9     sign strippers: |K| and |Q| of each stage into one of two copy buffers
-constexpr int TH_TILE = 128;
-constexpr int TH_N = 16;                  // MMA N: the group's query heads, padded
-constexpr int TH_STAGES = 4;
-constexpr int TH_ACC = 4;                 // TMEM accumulator pairs (D1, D2), TH_N columns each
-constexpr int TH_KBYTES = TH_TILE * 128;  // one 64-dim half of the K tile
-constexpr int TH_QBYTES = TH_N * 128;     // one 64-dim half of the query rows
-constexpr int TH_STAGE = 2 * (TH_KBYTES + TH_QBYTES);  // head_dim 128
-constexpr int TH_THREADS = 320;
-constexpr int TH_LIST = 1024;             // fixup list capacity (128 positions x 8 heads)
-
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-__device__ __forceinline__ void abs_sync() { asm volatile("bar.sync 2, 128;" ::: "memory"); }
-
-// A barrier of the 128 threads on named barrier `id` that returns, in each of them, whether `v`
-// held in all: the exit decisions after bounded waits stay uniform over the warps that share the
-// barrier.
-__device__ __forceinline__ bool all128(int id, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.and.pred q, %2, 128, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "r"(id)
-        : "memory");
-    return r != 0;
-}
-
-// bf16 element d of row r of a [rows][128] tile stored as two 64-column halves in the 128-byte
-// swizzle (half h at base + h * half_bytes; 16-byte chunk c of row r at chunk c ^ (r % 8))
-__device__ __forceinline__ float swz_elem(const unsigned char *base, int half_bytes, int r, int d) {
-    const int h = d >> 6, c = (d & 63) >> 3, e = d & 7;
-    const bf16 *p = reinterpret_cast<const bf16 *>(base + h * half_bytes + r * 128 + ((c ^ (r & 7)) << 4)) + e;
-    return __bfloat162float(*p);
-}
-
-template <int NREP>
-__global__ void __launch_bounds__(TH_THREADS, 1)
-    attn_scores_hyb_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQ,
-                           const __grid_constant__ AttnArgs a, const __grid_constant__ ScoreXPlan pl, uint32_t idesc) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *abuf = smem + (size_t)TH_STAGES * TH_STAGE;  // [2] sign-stripped copies, same layout
-    uint64_t *full = reinterpret_cast<uint64_t *>(abuf + 2 * TH_STAGE);
-    uint64_t *empty = full + TH_STAGES;       // MMA reads, stripper reads and epilogue fixups done
-    uint64_t *abs_full = empty + TH_STAGES;   // [2]
-    uint64_t *abs_empty = abs_full + 2;       // [2]
-    uint64_t *acc_full = abs_empty + 2;       // [TH_ACC]
-    uint64_t *acc_empty = acc_full + TH_ACC;  // [TH_ACC]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + TH_ACC);
-    int *list_n = reinterpret_cast<int *>(tmem_slot + 4);
-    unsigned short *list = reinterpret_cast<unsigned short *>(list_n + 4);  // (row << 3) | head
-    int *prefix = reinterpret_cast<int *>(list + TH_LIST);
-    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
-    if (threadIdx.x == 0) {
-        for (int i = 0; i < TH_STAGES; i++) {
-            mbar_init(&full[i], 1);
-            mbar_init(&empty[i], 3);
-        }
-        for (int i = 0; i < 2; i++) {
-            mbar_init(&abs_full[i], 1);
-            mbar_init(&abs_empty[i], 1);
-        }
-        for (int i = 0; i < TH_ACC; i++) {
-            mbar_init(&acc_full[i], 1);
-            mbar_init(&acc_empty[i], 128);
-        }
-        fence_barrier_init();
-        prefetch_tmap(&tmK);
-        prefetch_tmap(&tmQ);
-    }
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(2 * TH_ACC * TH_N)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-    }
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem_base = *tmem_slot;
-    pdl_trigger();
-    pdl_wait();  // positions, queries and the newest cache rows come from the previous kernels
-    const int total = build_prefix(a, TH_TILE, prefix);
-    const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
-    const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
-    const int n = i1 - i0;
-    int cur = n > 0 ? first_seq(prefix, a.B, i0) : 0;  // this thread's sequence cursor
-
-    if (warp == 0 && lane == 0) {
-        // ---------------- producer
-        const uint64_t stream_pol = policy_evict_first();
-        int k = 0;
-        for (; k < n; k++) {
-            const int st = k % TH_STAGES;
-            if (k >= TH_STAGES && !mbar_wait(&empty[st], ((k / TH_STAGES) - 1) & 1, &g_dev_error)) break;
-            const Item it = item_at(a, prefix, TH_TILE, i0 + k, cur);
-            unsigned char *base = smem + (size_t)st * TH_STAGE;
-            mbar_arrive_expect_tx(&full[st], (uint32_t)TH_STAGE);
-            const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * TH_TILE;
-            const int qrow = it.b * a.n_heads + it.kvh * NREP;
-            for (int h = 0; h < 2; h++) {
-                tma_load_2d_stream(base + h * TH_KBYTES, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow, &full[st],
-                                   stream_pol);
-                tma_load_2d(base + 2 * TH_KBYTES + h * TH_QBYTES, &tmQ, h * TMA_BK, qrow, &full[st]);
-            }
-        }
-        for (int j = max(0, k - TH_STAGES); j < k; j++) mbar_wait(&full[j % TH_STAGES], (j / TH_STAGES) & 1, &g_dev_error);
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer
-        for (int k = 0; k < n; k++) {
-            const int st = k % TH_STAGES, buf = k % TH_ACC, ab = k & 1;
-            if (k >= TH_ACC && !mbar_wait(&acc_empty[buf], ((k / TH_ACC) - 1) & 1, &g_dev_error)) break;
-            if (!mbar_wait(&full[st], (k / TH_STAGES) & 1, &g_dev_error)) break;
-            tc_fence_after();
-            const uint32_t kb = smem_u32(smem + (size_t)st * TH_STAGE), qb = kb + 2 * TH_KBYTES;
-            const uint32_t d1 = tmem_base + buf * 2 * TH_N, d2 = d1 + TH_N;
-            for (int kk = 0; kk < 8; kk++) {
-                const int h = kk >> 2, o = (kk & 3) * 32;
-                mma_bf16(d1, smem_desc_sw128(kb + h * TH_KBYTES + o), smem_desc_sw128(qb + h * TH_QBYTES + o), idesc,
-                         kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&empty[st]);  // the MMA's reads of the stage are done once these complete
-            if (!mbar_wait(&abs_full[ab], (k >> 1) & 1, &g_dev_error)) break;
-            tc_fence_after();
-            const uint32_t akb = smem_u32(abuf + (size_t)ab * TH_STAGE), aqb = akb + 2 * TH_KBYTES;
-            for (int kk = 0; kk < 8; kk++) {
-                const int h = kk >> 2, o = (kk & 3) * 32;
-                mma_bf16(d2, smem_desc_sw128(akb + h * TH_KBYTES + o), smem_desc_sw128(aqb + h * TH_QBYTES + o), idesc,
-                         kk > 0 ? 1u : 0u);
-            }
-            mma_commit(&abs_empty[ab]);
-            mma_commit(&acc_full[buf]);
-        }
-    } else if (warp >= 6) {
-        // ---------------- sign strippers: the stage's K and query tiles with bit 15 of every bf16 cleared
-        const int t = threadIdx.x - 192;
-        for (int k = 0; k < n; k++) {
-            const int st = k % TH_STAGES, ab = k & 1;
-            bool ok = mbar_wait(&full[st], (k / TH_STAGES) & 1, &g_dev_error);
-            if (ok && k >= 2) ok = mbar_wait(&abs_empty[ab], ((k >> 1) - 1) & 1, &g_dev_error);
-            ok = all128(2, ok);
-            const uint4 *src = reinterpret_cast<const uint4 *>(smem + (size_t)st * TH_STAGE);
-            uint4 *dst = reinterpret_cast<uint4 *>(abuf + (size_t)ab * TH_STAGE);
-            if (ok)
-                for (int i = t; i < TH_STAGE / 16; i += 128) {
-                    uint4 v = src[i];
-                    v.x &= 0x7FFF7FFFu;
-                    v.y &= 0x7FFF7FFFu;
-                    v.z &= 0x7FFF7FFFu;
-                    v.w &= 0x7FFF7FFFu;
-                    dst[i] = v;
-                }
-            fence_proxy_async();  // the tensor core reads the copy through the async proxy
-            abs_sync();
-            if (t == 0) {
-                mbar_arrive(&abs_full[ab]);
-                mbar_arrive(&empty[st]);
-            }
-            if (!ok) break;
-        }
-    } else if (warp >= 2) {
-        // ---------------- epilogue: thread = position row of the tile
-        const int quarter = warp % 4;
-        const int row = quarter * 32 + lane;
-        const int et = threadIdx.x - 64;  // 0..127
-        const uint32_t lane_addr = tmem_base + ((uint32_t)(quarter * 32) << 16);
-        for (int k = 0; k < n; k++) {
-            const int st = k % TH_STAGES, buf = k % TH_ACC;
-            if (!all128(1, mbar_wait(&acc_full[buf], (k / TH_ACC) & 1, &g_dev_error))) break;
-            tc_fence_after();
-            float d1[8], d2[8];
-            tmem_ld8(lane_addr + buf * 2 * TH_N, d1);
-            tmem_ld8(lane_addr + buf * 2 * TH_N + TH_N, d2);
-            tmem_wait_ld();
-            tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
-            const Item it = item_at(a, prefix, TH_TILE, i0 + k, cur);
-            const int t = it.c * TH_TILE + row;
-            float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
-            if (et == 0) *list_n = 0;
-            epi_sync();
-            if (t < it.len) {
-#pragma unroll
-                for (int h = 0; h < NREP; h++) {
-                    const float e = 0x1p-14f * d2[h];
-                    const float lo = __fsub_rd(d1[h], e), hi = __fadd_ru(d1[h], e);
-                    const float r = round_bf16(d1[h]);
-                    if (round_bf16(lo) == r && round_bf16(hi) == r && e == e) {
-                        sc[(size_t)h * a.ld + t] = round_bf16(r * a.scale);
-                    } else {
-                        const int slot = atomicAdd(list_n, 1);
-                        list[slot] = (unsigned short)((row << 3) | h);
-                    }
-                }
-            }
-            epi_sync();
-            // the listed dots, recomputed in the reference's order from the stage's tiles
-            const int m = *list_n;
-            const unsigned char *kt = smem + (size_t)st * TH_STAGE, *qt = kt + 2 * TH_KBYTES;
-            for (int i = et; i < m; i += 128) {
-                const int r_ = list[i] >> 3, h = list[i] & 7;
-                float dot = 0.0f;
-                for (int d = 0; d < 128; d++) dot = __fmaf_rn(swz_elem(qt, TH_QBYTES, h, d), swz_elem(kt, TH_KBYTES, r_, d), dot);
-                sc[(size_t)h * a.ld + it.c * TH_TILE + r_] = round_bf16(round_bf16(dot) * a.scale);
-            }
-            epi_sync();
-            if (et == 0) mbar_arrive(&empty[st]);
-        }
-    }
-    __syncwarp();
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(2 * TH_ACC * TH_N)
-                     : "memory");
-    }
-}
-
 // ------------------------------------------------------------------ pv on tcgen05 (split mode)
 // One item = (b, kv head, chunk of positions); per 128-position tile the MMA computes
 // D[head_dim x 16] += V_tile^T[head_dim x 128] . P^T[128 x 16] into a TMEM accumulator.
@@ -1352,34 +1110,6 @@ int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
     return Q3_OK;
 }
 
-// head_dim 128, packed queries (the query map is [B * n_heads][128]), and few enough sequences for
-// the item table beside the rings
-bool scores_hybrid_ok(const AttnArgs &a) {
-    return a.head_dim == 128 && a.q_stride == (long long)a.n_heads * a.head_dim && a.B <= 512;
-}
-
-template <int NREP>
-int launch_scores_hyb(const AttnArgs &a, cudaStream_t s) {
-    ScoreXPlan pl;
-    pl.halves = 2;
-    pl.k_rows_per_seq = (int)(a.kv.seq / a.kv.pos);
-    pl.k_rows_per_head = a.kv.head >= a.kv.pos ? (int)(a.kv.head / a.kv.pos) : 0;
-    pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
-    // kind::f16: fp32 accumulate, bf16 A and B, both K-major, N = 16, M = 128
-    const uint32_t idesc =
-        (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TH_N >> 3) << 17) | ((uint32_t)(TH_TILE >> 4) << 24);
-    CUtensorMap mk, mq;
-    if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, TH_TILE)) return Q3_ERR_ARG;
-    if (!make_map_strided(&mq, a.q, (long long)a.B * a.n_heads, a.head_dim, a.head_dim, TH_N)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)(TH_STAGES + 2) * TH_STAGE + (2 * TH_STAGES + 4 + 2 * TH_ACC) * 8 + 32 +
-                        TH_LIST * 2 + (size_t)PREFIX_INTS(a.B) * 4;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_hyb_kernel<NREP>), smem));
-    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + TH_TILE - 1) / TH_TILE);
-    const int grid = (int)std::min<long long>(max_items, num_sms());
-    Q3_TRY_LAUNCH(launch(attn_scores_hyb_kernel<NREP>, dim3(grid), dim3(TH_THREADS), smem, s, 1, mk, mq, a, pl, idesc));
-    return Q3_OK;
-}
-
 // One block of 128 * NREP threads per (sequence, kv head).
 template <int NREP>
 int launch_stats(const AttnArgs &a, cudaStream_t s) {
@@ -1406,9 +1136,8 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
     return Q3_OK;
 }
 
-// The TMA-fed scores need whole 64-dim halves and contiguous per-sequence caches in kv_dim rows
-// (the tensor-core variant also a packed q, scores_hybrid_ok); the vectorized pv needs an even
-// head_dim that splits 128 threads into groups.
+// The TMA-fed scores need whole 64-dim halves and contiguous per-sequence caches in kv_dim rows;
+// the vectorized pv needs an even head_dim that splits 128 threads into groups.
 bool split_fast_path(const AttnArgs &a) {
     const KvLayout &kv = a.kv;
     const bool heads_in_row = kv.head < kv.pos;  // reference layout
@@ -1424,7 +1153,7 @@ int launch_nrep(const AttnArgs &a, int dpt, cudaStream_t s) {
     const bool split = a.stats != nullptr;
     const size_t prefix_bytes = (size_t)PREFIX_INTS(a.B) * 4;
     if (split && split_fast_path(a)) {
-        int st = scores_hybrid_ok(a) ? launch_scores_hyb<NREP>(a, s) : launch_scores_exact<NREP>(a, s);
+        int st = launch_scores_exact<NREP>(a, s);
         if (st != Q3_OK) return st;
         st = launch_stats<NREP>(a, s);
         if (st != Q3_OK) return st;

@@ -275,9 +275,8 @@ def test_engine_batch1_qwen3_4b_slice_to_position_8191(path):
 def test_split_scores_bit_identical_to_serial_dot(case):
     """The split path's scores (scratch offset 0, [B][n_heads][ld] fp32) against the CPU oracle's
     serial fused multiply-add chain (the reference's scores), every valid (sequence, head,
-    position) bit for bit. At head_dim 128 they come from the tensor cores with the exact
-    recomputation of every dot that lies near a bf16 rounding boundary; "large" scales K so that
-    the products and their bound grow, "edges" has positions 0, 1, 127, 128 and 255."""
+    position) bit for bit: attn_scores_exact_kernel keeps the reference's serial chain on the CUDA
+    cores. "large" scales K up, "edges" has positions 0, 1, 127, 128 and 255 (tile edges)."""
     n_heads, n_kv, hd = 32, 8, 128
     if case == "config4":
         positions, max_seq, kscale = np.linspace(3900, 4200, 6).astype(int).tolist(), 4224, 1.0
