@@ -17,6 +17,7 @@ Extra keys on the same line (the other BASELINE configurations):
           pre-filled to 2048, the whole job's tokens/s (strong scaling).
   batch1  configuration 3 (N = 1): Qwen3-4B at batch 1, tokens/s and HBM fraction at positions
           256, 2048 and 8192.
+  prefill (N = 1) prompt prefill of one Qwen3-4B sequence, 2048 tokens in 64-row passes.
   dropin  (N = 1) the reference's own host program, unchanged, linked against this library,
           on its own --bench protocol (src/main.cu:110-148) with a Qwen3-4B checkpoint written
           to disk; and the load time of that checkpoint by the reference's loader (the same
@@ -309,6 +310,7 @@ def run_mine(args) -> dict | None:
         line["strong"] = strong
     if n == 1 and not args.no_extra:
         line["batch1"] = batch1_leg(weights, args, hbm, hbm_src)
+        line["prefill"] = prefill_leg(weights)
         line["dropin"] = dropin_leg(weights, hbm, hbm_src)
     del weights
     dist.close()
@@ -466,6 +468,35 @@ def batch1_leg(weights, args, hbm, hbm_src, megakernel: bool = False) -> dict:
             "path": "one persistent kernel per token" if megakernel else "captured graph of per-op kernels",
             "steps": K, "warmup": W, "positions": per_pos, "e2e_at_2048": e2e, "gpu_launches_per_token": launches,
             "peak": hbm, "peak_source": hbm_src}
+
+
+PREFILL_TOKENS = 2048
+PREFILL_ROWS = 64
+
+
+def prefill_leg(weights) -> dict:
+    """Prompt prefill (q3_engine_prefill) of one Qwen3-4B sequence: PREFILL_TOKENS random prompt
+    tokens in passes of PREFILL_ROWS rows (tcgen05 projections with N = rows; each row attends
+    causally over the sequence's cache). Timed from the host call to its return (the call waits
+    for its work), after one warm-up prefill. The reference runs a prompt one token per forward
+    (src/main.cu:122-124), i.e. at its decode rate."""
+    import time as _t
+
+    import numpy as np
+    import torch
+    from llm_inference_b200.engine import Engine
+    shape = weights.shape
+    eng = Engine(weights, batch=PREFILL_ROWS, max_seq=PREFILL_TOKENS + 64)
+    prompt = np.random.default_rng(5).integers(0, shape.vocab_size, PREFILL_TOKENS).tolist()
+    eng.prefill(0, prompt[:PREFILL_ROWS])  # warm-up
+    torch.cuda.synchronize()
+    t0 = _t.perf_counter()
+    eng.prefill(0, prompt)
+    sec = _t.perf_counter() - t0
+    eng.close()
+    return {"workload": f"Qwen3-4B, one sequence, {PREFILL_TOKENS} prompt tokens in passes of {PREFILL_ROWS} rows",
+            "seconds": round(sec, 4), "tok_s": round(PREFILL_TOKENS / sec, 1),
+            "timing": "host clock around q3_engine_prefill, which waits for its work"}
 
 
 def _run_logged(cmd, timeout):
