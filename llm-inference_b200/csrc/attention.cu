@@ -573,7 +573,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     attn_scores_exact_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ AttnArgs a,
                              const __grid_constant__ ScoreXPlan pl) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *smem = align_shared<1024>(smem_raw);
     const int hd = a.head_dim;
     float *q_all = reinterpret_cast<float *>(smem + (size_t)SX_STAGES * SX_BOX);  // [SX_GROUPS][hd][NREP]
     uint64_t *full = reinterpret_cast<uint64_t *>(q_all + SX_GROUPS * NREP * hd);
@@ -731,7 +731,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
     attn_pv_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a,
                       const __grid_constant__ PvTcPlan pl) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *smem = align_shared<1024>(smem_raw);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)PV_STAGES * PV_STAGE_BYTES);
     uint64_t *pfull = full + PV_STAGES;
     uint64_t *empty = pfull + PV_STAGES;

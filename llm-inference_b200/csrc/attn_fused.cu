@@ -86,7 +86,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     constexpr int PV_HPT = (NREP + PV_HG - 1) / PV_HG;
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned base: the K boxes use the 128-byte swizzle
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *smem = align_shared<1024>(smem_raw);
     unsigned char *ks = smem;                                                   // [FA_STAGES][HALVES][FA_TILE][64], swizzled
     bf16 *vs = reinterpret_cast<bf16 *>(smem + FA_STAGES * KTILE_BYTES);       // [FA_STAGES][FA_TILE][HD]
     float *qf = reinterpret_cast<float *>(smem + FA_STAGES * (KTILE_BYTES + VTILE_BYTES));  // [NREP][HD] roped queries

@@ -37,6 +37,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// The dynamic shared-memory base rounded up to a multiple of A bytes (the swizzled TMA tiles
+// want 1024). The offset is added to the shared array's own pointer, so the compiler still
+// knows that every pointer derived from the result is in shared memory and emits shared loads.
+// Rounding through an integer cast would lose that, and every access would become a generic
+// load, which the hardware must resolve at run time.
+template <int A>
+__device__ __forceinline__ unsigned char *align_shared(unsigned char *base) {
+    return base + ((A - (smem_u32(base) & (A - 1))) & (A - 1));
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int NA = EPI == GATE_UP ? 2 : 1;  // weight tiles per stage (gate and up)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // 1024-byte aligned base for the swizzled tiles
-    unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *smem = align_shared<1024>(smem_raw);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)a.stages * a.stage_bytes);
     uint64_t *empty = full + a.stages;
     uint64_t *acc_full = empty + a.stages;
