@@ -521,10 +521,9 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 // flight, which is what keeps HBM busy -- and then computes, for each of its two rows and every
 // query head of the kv group, the reference's dot product: one fp32 chain per (row, head), dims
 // in order, one fused multiply-add each (src/kernels.cu:455-460, where nvcc fuses
-// `dot += q * k`), then s = round_bf16(round_bf16(dot) * scale). Each step is one mixed-precision
-// fma of the bf16 q and k into the fp32 chain (fma_pair), bit for bit the fp32 fma of the
-// converted operands. The group's query heads sit in shared memory as bf16 [dim][head], so one
-// vector load gives a dim's value for every head and serves both rows. The swizzle puts the 16-byte chunk c of row r at chunk c ^ (r % 8): a warp's
+// `dot += q * k`), then s = round_bf16(round_bf16(dot) * scale). The group's query heads sit in
+// shared memory as fp32 [dim][head], so one vector load gives a dim's value for every head and
+// serves both rows. The swizzle puts the 16-byte chunk c of row r at chunk c ^ (r % 8): a warp's
 // 32 threads reading the same logical chunk of 32 consecutive rows need only the four wavefronts
 // of their 512 bytes.
 constexpr int SX_TILE = 128;
@@ -559,73 +558,31 @@ __device__ __forceinline__ bool group_any(int group, bool v) {
     return r != 0;
 }
 
-// q values of one dim for the NREP heads, bf16 pairs (heads 2i, 2i + 1 in word i): one
-// shared-memory vector load. With one head the word holds it in its low half.
+// q values of one dim for the NREP heads: one shared-memory vector load
 template <int NREP>
-struct QWords {
-    uint32_t w[(NREP + 1) / 2];
+struct QVec {
+    float v[NREP];
 };
 template <int NREP>
-__device__ __forceinline__ QWords<NREP> load_q(const bf16 *p) {
-    QWords<NREP> q;
-    if constexpr (NREP == 8) {
-        const uint4 u = *reinterpret_cast<const uint4 *>(p);
-        q.w[0] = u.x;
-        q.w[1] = u.y;
-        q.w[2] = u.z;
-        q.w[3] = u.w;
-    } else if constexpr (NREP == 4) {
-        const uint2 u = *reinterpret_cast<const uint2 *>(p);
-        q.w[0] = u.x;
-        q.w[1] = u.y;
+__device__ __forceinline__ QVec<NREP> load_q(const float *p) {
+    QVec<NREP> q;
+    if constexpr (NREP % 4 == 0) {
+#pragma unroll
+        for (int i = 0; i < NREP; i += 4) {
+            const float4 f = *reinterpret_cast<const float4 *>(p + i);
+            q.v[i] = f.x;
+            q.v[i + 1] = f.y;
+            q.v[i + 2] = f.z;
+            q.v[i + 3] = f.w;
+        }
     } else if constexpr (NREP == 2) {
-        q.w[0] = *reinterpret_cast<const uint32_t *>(p);
+        const float2 f = *reinterpret_cast<const float2 *>(p);
+        q.v[0] = f.x;
+        q.v[1] = f.y;
     } else {
-        q.w[0] = *reinterpret_cast<const unsigned short *>(p);
+        q.v[0] = p[0];
     }
     return q;
-}
-
-// acc0 = fma(q.lo, k, acc0) and acc1 = fma(q.hi, k, acc1), k the low (KHI false) or high half
-// of `k2`. sm_100's mixed-precision fma takes the bf16 operands as they are: their product is
-// exact in fp32 (8 + 8 significant bits), and the one rounding of q * k + acc is that of
-// fmaf(float(q), float(k), acc), so no operand is converted to fp32 first.
-template <bool KHI>
-__device__ __forceinline__ void fma_pair(float &acc0, float &acc1, uint32_t q2, uint32_t k2) {
-    if constexpr (KHI)
-        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
-            "fma.rn.f32.bf16 %0, ql, kh, %0;\n\tfma.rn.f32.bf16 %1, qh, kh, %1;\n\t}"
-            : "+f"(acc0), "+f"(acc1)
-            : "r"(q2), "r"(k2));
-    else
-        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
-            "fma.rn.f32.bf16 %0, ql, kl, %0;\n\tfma.rn.f32.bf16 %1, qh, kl, %1;\n\t}"
-            : "+f"(acc0), "+f"(acc1)
-            : "r"(q2), "r"(k2));
-}
-template <bool KHI>
-__device__ __forceinline__ void fma_one(float &acc, uint32_t q2, uint32_t k2) {
-    if constexpr (KHI)
-        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %1;\n\tmov.b32 {kl, kh}, %2;\n\t"
-            "fma.rn.f32.bf16 %0, ql, kh, %0;\n\t}"
-            : "+f"(acc)
-            : "r"(q2), "r"(k2));
-    else
-        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %1;\n\tmov.b32 {kl, kh}, %2;\n\t"
-            "fma.rn.f32.bf16 %0, ql, kl, %0;\n\t}"
-            : "+f"(acc)
-            : "r"(q2), "r"(k2));
-}
-
-// The NREP chains of one row take dim e of a chunk (e odd: the high half of K word e / 2).
-template <int NREP, bool KHI>
-__device__ __forceinline__ void fma_heads(float (&acc)[NREP], const QWords<NREP> &q, uint32_t kw) {
-    if constexpr (NREP == 1) {
-        fma_one<KHI>(acc[0], q.w[0], kw);
-    } else {
-#pragma unroll
-        for (int i = 0; i < NREP / 2; i++) fma_pair<KHI>(acc[2 * i], acc[2 * i + 1], q.w[i], kw);
-    }
 }
 
 template <int NREP>
@@ -685,7 +642,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     // ---------------- consumers: group g takes items g, g + SX_GROUPS, ...
     const int group = (warp - 1) / SX_GWARPS;
     const int gt = threadIdx.x - 32 - group * SX_GWARPS * 32;  // 0..63
-    bf16 *q_s = reinterpret_cast<bf16 *>(q_all + group * NREP * hd);  // [hd][NREP] (half the region)
+    float *q_s = q_all + group * NREP * hd;                    // [hd][NREP]
     int qb = -1, qk = -1;
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
@@ -697,7 +654,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
         if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
             group_sync(group);             // nobody still reads the previous ones
             const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
-            for (int j = gt; j < NREP * hd; j += SX_GWARPS * 32) q_s[(j % hd) * NREP + j / hd] = qg[j];
+            for (int j = gt; j < NREP * hd; j += SX_GWARPS * 32) q_s[(j % hd) * NREP + j / hd] = __bfloat162float(qg[j]);
             group_sync(group);
             qb = it.b;
             qk = it.kvh;
@@ -728,20 +685,19 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);  // the rows are in registers: the box is free
             if (failed) break;
-            const bf16 *qd = q_s + half * 64 * NREP;
+            const float *qd = q_s + half * 64 * NREP;
 #pragma unroll
             for (int c = 0; c < 8; c++) {
-                const uint4 wa = *reinterpret_cast<const uint4 *>(&ka[c]);
-                const uint4 wb = *reinterpret_cast<const uint4 *>(&kb[c]);
-                const uint32_t pa[4] = {wa.x, wa.y, wa.z, wa.w}, pb[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-                for (int e = 0; e < 8; e += 2) {
-                    const QWords<NREP> q0 = load_q<NREP>(qd + (c * 8 + e) * NREP);
-                    const QWords<NREP> q1 = load_q<NREP>(qd + (c * 8 + e + 1) * NREP);
-                    fma_heads<NREP, false>(acc_a, q0, pa[e / 2]);
-                    fma_heads<NREP, false>(acc_b, q0, pb[e / 2]);
-                    fma_heads<NREP, true>(acc_a, q1, pa[e / 2]);
-                    fma_heads<NREP, true>(acc_b, q1, pb[e / 2]);
+                for (int e = 0; e < 8; e++) {
+                    const QVec<NREP> q = load_q<NREP>(qd + (c * 8 + e) * NREP);
+                    const float fa = e & 1 ? __high2float(ka[c].h[e / 2]) : __low2float(ka[c].h[e / 2]);
+                    const float fb = e & 1 ? __high2float(kb[c].h[e / 2]) : __low2float(kb[c].h[e / 2]);
+#pragma unroll
+                    for (int h = 0; h < NREP; h++) {
+                        acc_a[h] = __fmaf_rn(q.v[h], fa, acc_a[h]);
+                        acc_b[h] = __fmaf_rn(q.v[h], fb, acc_b[h]);
+                    }
                 }
             }
         }
