@@ -42,7 +42,7 @@ constexpr int GV_THREADS_RESIDUAL = 128;
 #define Q3_GEMV_LONG_ROWS 1
 #endif
 // UR: chunk rounds (one 16-byte chunk per lane each) per batch and row; a unit's batch holds
-// RPU * UR chunks per lane. The host picks the smallest UR in {8, 12, 16} that covers a row in
+// RPU * UR chunks per lane. The host picks the smallest UR in {8, 10, 12, 16} that covers a row in
 // one batch, else 16 (8 for gate_up, whose batches hold two rows).
 
 enum Epi : int { PLAIN = 0, RESIDUAL = 1, QKV = 2, GATE_UP = 3 };
@@ -231,6 +231,9 @@ int launch_gemv(GemvArgs a, cudaStream_t stream) {
     if (a.norm_w && (a.cols > GV_NORM_MAX_COLS || (reinterpret_cast<uintptr_t>(a.norm_w) & 15))) return Q3_ERR_SHAPE;
     const int rounds = (a.cols / 8 + 31) / 32;
     if (rounds <= 8) return launch_gemv_ur<EPI, 8>(a, stream);
+    // 2560-wide rows (Qwen3-4B's hidden size) take 10 rounds: a batch of exactly 10 keeps gate_up at
+    // 117 registers, two CTAs (16 warps) per SM instead of one, and qkv and the LM head at three
+    if (rounds <= 10) return launch_gemv_ur<EPI, 10>(a, stream);
     if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
     if constexpr (EPI == RESIDUAL) {
         if (rounds <= 16) return launch_gemv_ur<EPI, 16, false, 5>(a, stream);
