@@ -150,23 +150,6 @@ __device__ __forceinline__ Item item_at(const AttnArgs &a, const int *prefix, in
     return it;
 }
 
-// The item after `it`, without item_at's divisions and table walk: a lone producer thread
-// issuing a box every few hundred cycles cannot afford them next to warps that keep its
-// scheduler busy. Past the last item `it.b` becomes B and nothing more is read.
-__device__ __forceinline__ void item_next(const AttnArgs &a, const int *prefix, int chunk, Item &it) {
-    if (++it.c < it.nc) return;
-    it.c = 0;
-    if (++it.kvh < a.n_kv) return;
-    it.kvh = 0;
-    int b = it.b + 1;
-    while (b < a.B && prefix[b + 1] == prefix[b]) b++;  // sequences without items
-    it.b = b;
-    if (b < a.B) {
-        it.len = prefix[a.B + 1 + b];
-        it.nc = (it.len + chunk - 1) / chunk;
-    }
-}
-
 // Copies n scores (floats) from global to shared memory as cp.async groups' members.
 __device__ __forceinline__ void stage_scores(float *dst, const float *src, int n) {
     if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
@@ -620,14 +603,12 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
             // ---------------- producer: box j of the ring is box j % halves of item j / halves
             const uint64_t stream_pol = policy_evict_first();  // K rows are read once per step
             const int nbox = n * pl.halves;
-            Item it = {};
-            if (n > 0) it = item_at(a, prefix, SX_TILE, i0, cur);
             int j = 0;
             for (; j < nbox; j++) {
                 const int st = j % SX_STAGES;
                 if (j >= SX_STAGES && !mbar_wait(&empty[st], ((j / SX_STAGES) - 1) & 1, &g_dev_error)) break;
                 const int h = j % pl.halves;
-                if (h == 0 && j > 0) item_next(a, prefix, SX_TILE, it);
+                const Item it = item_at(a, prefix, SX_TILE, i0 + j / pl.halves, cur);
                 mbar_arrive_expect_tx(&full[st], (uint32_t)SX_BOX);
                 const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * SX_TILE;
                 tma_load_2d_stream(smem + (size_t)st * SX_BOX, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow,
@@ -646,11 +627,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     int qb = -1, qk = -1;
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
-    Item it = {};
-    if (group < n) it = item_at(a, prefix, SX_TILE, i0 + group, cur);
     for (int k = group; k < n && !failed; k += SX_GROUPS) {
-        if (k > group)
-            for (int i = 0; i < SX_GROUPS; i++) item_next(a, prefix, SX_TILE, it);
+        const Item it = item_at(a, prefix, SX_TILE, i0 + k, cur);
         if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
             group_sync(group);             // nobody still reads the previous ones
             const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
@@ -802,8 +780,6 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     int cur = i1 > i0 ? first_seq(prefix, a.B, i0) : 0;
-    Item walk = {};  // every role walks the CTA's items in order
-    if (i1 > i0) walk = item_at(a, prefix, chunk, i0, cur);
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer: V tile halves by TMA, the group's scores by bulk copy
@@ -811,8 +787,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++) {
-            if (item > i0) item_next(a, prefix, chunk, walk);
-            const Item it = walk;
+            const Item it = item_at(a, prefix, chunk, item, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
             const int row0 = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head;
@@ -842,13 +817,17 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         }
         // drain: every issued copy lands before the CTA exits
         for (int j = max(0, k - PV_STAGES); j < k; j++) mbar_wait(&full[j % PV_STAGES], (j / PV_STAGES) & 1, &g_dev_error);
+        // tail: the MMA frees each stage with tcgen05.commit, whose arrive on `empty` is performed
+        // asynchronously when the MMAs finish -- possibly after the accumulator's own commit, which
+        // is all the epilogue waits for. Wait for the last uses' arrives too, so that none lands in
+        // the shared memory of the next CTA on this SM.
+        for (int j = max(0, k - PV_STAGES); j < k; j++) mbar_wait(&empty[j % PV_STAGES], (j / PV_STAGES) & 1, &g_dev_error);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            if (item > i0) item_next(a, prefix, chunk, walk);
-            const Item it = walk;
+            const Item it = item_at(a, prefix, chunk, item, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const int buf = n_items % PV_ACC;
             if (n_items >= PV_ACC && !mbar_wait(&acc_empty[buf], ((n_items / PV_ACC) - 1) & 1, &g_dev_error)) break;
@@ -911,8 +890,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            if (item > i0) item_next(a, prefix, chunk, walk);
-            const Item it = walk;
+            const Item it = item_at(a, prefix, chunk, item, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             float m[NREP], sum[NREP];
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {

@@ -272,6 +272,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
         // leave no copy in flight into this CTA's shared memory
         for (int j = max(0, it - S); j < it; j++) mbar_wait(&full[j % S], (j / S) & 1, &g_dev_error);
+        // nor an arrive: the MMA frees each stage with tcgen05.commit, whose arrive on `empty` is
+        // performed asynchronously when the MMAs finish, possibly after the accumulator's commit that
+        // the epilogue waits for. Wait for the last stages' arrives as well.
+        for (int j = max(0, it - S); j < it; j++) mbar_wait(&empty[j % S], (j / S) & 1, &g_dev_error);
         if (res_load) mbar_wait(res_full, 0, &g_dev_error);
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer
