@@ -150,6 +150,44 @@ __device__ __forceinline__ Item item_at(const AttnArgs &a, const int *prefix, in
     return it;
 }
 
+// The CTA's items [i0, i0 + n) as a table in shared memory, filled by all threads at once:
+// (b | kvh << 16, c | nc << 16) per item. The split kernels' producer is one thread issuing a copy
+// every few hundred cycles next to warps that keep its scheduler busy; computing each item there
+// (a search over the sequences, a division) made it fall behind, the table makes an item one
+// shared-memory load. `cap` is the table's size; a CTA with more items, or items whose fields do
+// not fit 16 bits, computes them with item_at instead (fill_items returns false).
+__device__ bool fill_items(const AttnArgs &a, const int *prefix, int chunk, int i0, int n, int2 *tab, int cap) {
+    const bool fits = n <= cap && (a.max_seq + chunk - 1) / chunk < 65536 && a.B <= 65536 && a.n_kv <= 65536;
+    if (fits)
+        for (int k = threadIdx.x; k < n; k += blockDim.x) {
+            int b = first_seq(prefix, a.B, i0 + k);
+            const Item it = item_at(a, prefix, chunk, i0 + k, b);
+            tab[k] = make_int2(it.b | (it.kvh << 16), it.c | (it.nc << 16));
+        }
+    __syncthreads();
+    return fits;
+}
+
+// Item i0 + k: from the table when it holds the CTA's items, else computed (`cur` is the caller's
+// sequence cursor for item_at, and k must increase from call to call).
+__device__ __forceinline__ Item item_k(const AttnArgs &a, const int *prefix, int chunk, const int2 *tab, bool tabbed,
+                                       int i0, int k, int &cur) {
+    if (!tabbed) return item_at(a, prefix, chunk, i0 + k, cur);
+    const int2 v = tab[k];
+    Item it;
+    it.b = (int)((unsigned)v.x & 0xffffu);
+    it.kvh = (int)((unsigned)v.x >> 16);
+    it.c = (int)((unsigned)v.y & 0xffffu);
+    it.nc = (int)((unsigned)v.y >> 16);
+    it.len = prefix[a.B + 1 + it.b];
+    return it;
+}
+
+// Offset (in ints) of the item table after a PREFIX_INTS(B) prefix table: 8-byte aligned.
+#define ITEM_TAB_OFF(B) ((PREFIX_INTS(B) + 1) / 2 * 2)
+constexpr int ITEM_TAB_MAX = 1024;
+constexpr size_t SMEM_CTA_MAX = 232448;  // dynamic shared memory a CTA may opt in to on sm_100
+
 // Copies n scores (floats) from global to shared memory as cp.async groups' members.
 __device__ __forceinline__ void stage_scores(float *dst, const float *src, int n) {
     if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
@@ -521,6 +559,7 @@ struct ScoreXPlan {
     int k_rows_per_seq;   // rows of the K map per sequence (kv.seq / kv.pos)
     int k_rows_per_head;  // head-major caches: rows per kv head (kv.head / kv.pos), else 0
     int k_cols_per_head;  // heads within a row: columns per kv head (kv.head), else 0
+    int tab_cap;          // items the shared-memory item table holds
 };
 
 __device__ __forceinline__ void group_sync(int group) {
@@ -596,6 +635,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     const int n = i1 - i0;
+    int2 *tab = reinterpret_cast<int2 *>(prefix + ITEM_TAB_OFF(a.B));
+    const bool tabbed = fill_items(a, prefix, SX_TILE, i0, n, tab, pl.tab_cap);
     int cur = n > 0 ? first_seq(prefix, a.B, i0) : 0;  // this thread's sequence cursor
 
     if (warp == 0) {
@@ -608,7 +649,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                 const int st = j % SX_STAGES;
                 if (j >= SX_STAGES && !mbar_wait(&empty[st], ((j / SX_STAGES) - 1) & 1, &g_dev_error)) break;
                 const int h = j % pl.halves;
-                const Item it = item_at(a, prefix, SX_TILE, i0 + j / pl.halves, cur);
+                const Item it = item_k(a, prefix, SX_TILE, tab, tabbed, i0, j / pl.halves, cur);
                 mbar_arrive_expect_tx(&full[st], (uint32_t)SX_BOX);
                 const int krow = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head + it.c * SX_TILE;
                 tma_load_2d_stream(smem + (size_t)st * SX_BOX, &tmK, it.kvh * pl.k_cols_per_head + h * TMA_BK, krow,
@@ -628,7 +669,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
     for (int k = group; k < n && !failed; k += SX_GROUPS) {
-        const Item it = item_at(a, prefix, SX_TILE, i0 + k, cur);
+        const Item it = item_k(a, prefix, SX_TILE, tab, tabbed, i0, k, cur);
         if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
             group_sync(group);             // nobody still reads the previous ones
             const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
@@ -724,6 +765,7 @@ constexpr int PV_STAGE_BYTES = PV_T_OFF + 1024;             // the group's (max,
 struct PvTcPlan {
     int k_rows_per_seq, k_rows_per_head, k_cols_per_head;
     uint32_t idesc;
+    int tab_cap;  // items the shared-memory item table holds
 };
 
 template <int NREP>
@@ -779,6 +821,8 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
     const int total = build_prefix(a, chunk, prefix);
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    int2 *tab = reinterpret_cast<int2 *>(prefix + ITEM_TAB_OFF(a.B));
+    const bool tabbed = fill_items(a, prefix, chunk, i0, i1 - i0, tab, pl.tab_cap);
     int cur = i1 > i0 ? first_seq(prefix, a.B, i0) : 0;
 
     if (warp == 0 && lane == 0) {
@@ -787,7 +831,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++) {
-            const Item it = item_at(a, prefix, chunk, item, cur);
+            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
             const int row0 = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head;
@@ -827,7 +871,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            const Item it = item_at(a, prefix, chunk, item, cur);
+            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const int buf = n_items % PV_ACC;
             if (n_items >= PV_ACC && !mbar_wait(&acc_empty[buf], ((n_items / PV_ACC) - 1) & 1, &g_dev_error)) break;
@@ -890,7 +934,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            const Item it = item_at(a, prefix, chunk, item, cur);
+            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             float m[NREP], sum[NREP];
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
@@ -1106,8 +1150,10 @@ int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
     pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
     CUtensorMap mk;
     if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, SX_TILE)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)SX_GROUPS * NREP * a.head_dim * 4 +
-                        2 * SX_STAGES * 8 + (size_t)PREFIX_INTS(a.B) * 4;
+    const size_t base = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)SX_GROUPS * NREP * a.head_dim * 4 +
+                        2 * SX_STAGES * 8 + (size_t)ITEM_TAB_OFF(a.B) * 4;
+    pl.tab_cap = base < SMEM_CTA_MAX ? (int)std::min<size_t>(ITEM_TAB_MAX, (SMEM_CTA_MAX - base) / 8) : 0;
+    const size_t smem = base + (size_t)pl.tab_cap * 8;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_exact_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + SX_TILE - 1) / SX_TILE);
     const int grid = (int)std::min<long long>(max_items, num_sms());
@@ -1133,7 +1179,9 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
                ((uint32_t)(128 >> 4) << 24);
     CUtensorMap mv;
     if (!make_map_strided(&mv, a.vc, cache_map_rows(a), a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
-    const size_t smem = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)PREFIX_INTS(a.B) * 4;
+    const size_t base = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)ITEM_TAB_OFF(a.B) * 4;
+    pl.tab_cap = base < SMEM_CTA_MAX ? (int)std::min<size_t>(ITEM_TAB_MAX, (SMEM_CTA_MAX - base) / 8) : 0;
+    const size_t smem = base + (size_t)pl.tab_cap * 8;
     Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
     const int grid = (int)std::min<long long>(max_items, num_sms());
