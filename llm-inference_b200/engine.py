@@ -101,45 +101,58 @@ class DeviceWeights:
         return cls.from_tensors(shape, tensors, device)
 
     @classmethod
-    def load(cls, model_dir, device="cuda", staging_bytes: int = 64 << 20):
+    def load(cls, model_dir, device="cuda", staging_bytes: int = 32 << 20, threads: int | None = None):
         """from_checkpoint's result (the same device layout, bit for bit) without its host copies.
 
         The reference uploads each shard with one synchronous pageable cudaMemcpy after reading
-        the whole file (src/loader.cu:143-180). Here the safetensors headers are validated first
-        (checkpoint_layout), the files are memory-mapped, and every tensor streams through two
-        pinned staging buffers: while one buffer's chunk is copied to the device
-        (cudaMemcpyAsync on a dedicated stream), the next chunk is paged in and copied into the
-        other, so disk or page-cache reads overlap the DMA. Returns once the weights are on the
-        device."""
+        the whole file (src/loader.cu:143-180): one host thread, and the driver's own staging
+        between the page cache and the device. Here the safetensors headers are validated first
+        (checkpoint_layout) and the files are memory-mapped; the tensors, cut into chunks of at
+        most `staging_bytes` in file order, are dealt out to `threads` host threads. Each thread
+        owns two pinned staging buffers and a stream: it copies a chunk from the mapping into one
+        buffer (page-in and memcpy, with the GIL released) while the other buffer's chunk is in
+        flight to the device (cudaMemcpyAsync on its stream), so several page-cache reads and the
+        DMA run at once. Returns once the weights are on the device."""
+        import os
+        from concurrent.futures import ThreadPoolExecutor
+
         import torch
         shape, spans = ckpt.checkpoint_layout(model_dir)
         _, offsets, total = cls._layout(shape)
         blob = torch.zeros(total // 2, dtype=torch.int16, device=device)  # padding bytes are zero
         obj = cls(shape, blob, offsets)
         dst = blob.view(torch.uint8)
-        stream = torch.cuda.Stream(device=dst.device)
-        stream.wait_stream(torch.cuda.current_stream(dst.device))  # after the zero fill
-        stage = [torch.empty(staging_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
-        stage_np = [t.numpy() for t in stage]
-        done = [None, None]
+        dev = dst.device
         maps = {}
-        k = 0
-        for name, sp in sorted(spans.items(), key=lambda kv: (str(kv[1].path), kv[1].offset)):  # file order
+        chunks = []  # (file map, source offset, destination offset, bytes), in file order
+        for name, sp in sorted(spans.items(), key=lambda kv: (str(kv[1].path), kv[1].offset)):
             if sp.path not in maps:
                 maps[sp.path] = np.memmap(sp.path, dtype=np.uint8, mode="r")
-            src = maps[sp.path]
             for c0 in range(0, sp.nbytes, staging_bytes):
-                n = min(staging_bytes, sp.nbytes - c0)
-                buf = k % 2
-                if done[buf] is not None:
-                    done[buf].synchronize()  # the buffer's previous chunk has reached the device
-                np.copyto(stage_np[buf][:n], src[sp.offset + c0:sp.offset + c0 + n])
+                chunks.append((maps[sp.path], sp.offset + c0, offsets[name] + c0, min(staging_bytes, sp.nbytes - c0)))
+        n_threads = max(1, min(threads or min(8, os.cpu_count() or 1), len(chunks)))
+        stage_bytes = min(staging_bytes, max((c[3] for c in chunks), default=1))
+        torch.cuda.current_stream(dev).synchronize()  # the zero fill is done before any copy lands
+
+        def worker(t: int):
+            stream = torch.cuda.Stream(device=dev)
+            bufs = [torch.empty(stage_bytes, dtype=torch.uint8, pin_memory=True) for _ in range(2)]
+            views = [b.numpy() for b in bufs]
+            done = [None, None]
+            for k, (src, s0, d0, n) in enumerate(chunks[t::n_threads]):
+                i = k % 2
+                if done[i] is not None:
+                    done[i].synchronize()  # this buffer's previous chunk has reached the device
+                np.copyto(views[i][:n], src[s0:s0 + n])
                 with torch.cuda.stream(stream):
-                    dst[offsets[name] + c0:offsets[name] + c0 + n].copy_(stage[buf][:n], non_blocking=True)
-                    done[buf] = torch.cuda.Event()
-                    done[buf].record(stream)
-                k += 1
-        stream.synchronize()
+                    dst[d0:d0 + n].copy_(bufs[i][:n], non_blocking=True)
+                    done[i] = torch.cuda.Event()
+                    done[i].record(stream)
+            stream.synchronize()
+
+        with ThreadPoolExecutor(n_threads) as ex:
+            for f in [ex.submit(worker, t) for t in range(n_threads)]:
+                f.result()
         return obj
 
     @classmethod

@@ -138,7 +138,9 @@ def test_fast_loader_matches_plain_loader(tiny):
     torch = pytest.importorskip("torch")
     from llm_inference_b200.engine import DeviceWeights
     plain = DeviceWeights.from_checkpoint(tiny)
-    for staging in (64 << 20, 4096, 16000):  # one chunk per tensor, and chunks that split tensors
-        fast = DeviceWeights.load(tiny, staging_bytes=staging)
+    # one chunk per tensor, and chunks that split tensors; one host thread, and several that
+    # share out the chunks
+    for staging, threads in ((64 << 20, None), (4096, 1), (4096, 3), (16000, 8)):
+        fast = DeviceWeights.load(tiny, staging_bytes=staging, threads=threads)
         assert fast.offsets == plain.offsets
-        assert torch.equal(fast.blob, plain.blob), f"staging {staging}"
+        assert torch.equal(fast.blob, plain.blob), f"staging {staging}, threads {threads}"
