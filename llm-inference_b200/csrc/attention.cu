@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 // positions). A producer thread loads the item's K tile by TMA as head_dim / 64 boxes of
 // [128 positions][64 dims] (128-byte swizzle), one box per ring stage, into a ring of SX_STAGES
 // boxes, never waiting for anything but a free stage, so the cache streams while the dot products
-// run. Four groups of two consumer warps take the CTA's items in turn; in a group, thread r owns
+// run. G groups of two consumer warps take the CTA's items in turn; in a group, thread r owns
 // the positions r and r + 64 of the tile. For each box it copies its two rows' 128-byte pieces
 // into registers and frees the stage at once -- the ring then holds almost only copies in
 // flight, which is what keeps HBM busy -- and then computes, for each of its two rows and every
@@ -550,9 +550,18 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 constexpr int SX_TILE = 128;
 constexpr int SX_BOX = SX_TILE * 128;  // one 64-dim box: 16 KB
 constexpr int SX_STAGES = 12;
-constexpr int SX_GROUPS = 4;
-constexpr int SX_GWARPS = 2;                    // warps per group: 64 threads, two rows each
-constexpr int SX_THREADS = 32 + SX_GROUPS * SX_GWARPS * 32;  // producer warp + the consumer groups
+constexpr int SX_GWARPS = 2;  // warps per group: 64 threads, two rows each
+// Consumer groups per CTA, by boxes per item (head_dim / 64). A group waits on the ring stages of
+// its own items only, with the parity of the lap it expects; that is sound only if the stage's
+// previous box also belonged to this group (a box of another group may not have landed yet, and a
+// wait two phases ahead of the barrier passes at once). With items dealt round-robin that holds
+// when SX_STAGES is a multiple of groups x boxes per item: 6 groups for one or two boxes an item,
+// 4 for three (head_dim 192), 3 for four (head_dim 256).
+constexpr int sx_groups(int halves) { return halves == 4 ? 3 : halves == 3 ? 4 : 6; }
+static_assert(SX_STAGES % (sx_groups(1) * 1) == 0 && SX_STAGES % (sx_groups(2) * 2) == 0 &&
+                  SX_STAGES % (sx_groups(3) * 3) == 0 && SX_STAGES % (sx_groups(4) * 4) == 0,
+              "a ring stage must come back to the group that used it last");
+constexpr int sx_threads(int groups) { return 32 + groups * SX_GWARPS * 32; }  // producer warp + the groups
 
 struct ScoreXPlan {
     int halves;           // head_dim / 64: boxes per item
@@ -607,15 +616,15 @@ __device__ __forceinline__ QVec<NREP> load_q(const float *p) {
     return q;
 }
 
-template <int NREP>
-__global__ void __launch_bounds__(SX_THREADS, 1)
+template <int NREP, int G>
+__global__ void __launch_bounds__(sx_threads(G), 1)
     attn_scores_exact_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ AttnArgs a,
                              const __grid_constant__ ScoreXPlan pl) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = align_shared<1024>(smem_raw);
     const int hd = a.head_dim;
-    float *q_all = reinterpret_cast<float *>(smem + (size_t)SX_STAGES * SX_BOX);  // [SX_GROUPS][hd][NREP]
-    uint64_t *full = reinterpret_cast<uint64_t *>(q_all + SX_GROUPS * NREP * hd);
+    float *q_all = reinterpret_cast<float *>(smem + (size_t)SX_STAGES * SX_BOX);  // [G][hd][NREP]
+    uint64_t *full = reinterpret_cast<uint64_t *>(q_all + G * NREP * hd);
     uint64_t *empty = full + SX_STAGES;
     int *prefix = reinterpret_cast<int *>(empty + SX_STAGES);
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -661,14 +670,14 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
         }
         return;
     }
-    // ---------------- consumers: group g takes items g, g + SX_GROUPS, ...
+    // ---------------- consumers: group g takes items g, g + G, ...
     const int group = (warp - 1) / SX_GWARPS;
     const int gt = threadIdx.x - 32 - group * SX_GWARPS * 32;  // 0..63
     float *q_s = q_all + group * NREP * hd;                    // [hd][NREP]
     int qb = -1, qk = -1;
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
-    for (int k = group; k < n && !failed; k += SX_GROUPS) {
+    for (int k = group; k < n && !failed; k += G) {
         const Item it = item_k(a, prefix, SX_TILE, tab, tabbed, i0, k, cur);
         if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
             group_sync(group);             // nobody still reads the previous ones
@@ -1141,6 +1150,14 @@ long long cache_map_rows(const AttnArgs &a) {
     return a.kv.head >= a.kv.pos ? (long long)a.n_kv * (a.kv.head / a.kv.pos) : (long long)a.max_seq;
 }
 
+template <int NREP, int G>
+int launch_scores_exact_g(const CUtensorMap &mk, const AttnArgs &a, const ScoreXPlan &pl, int grid, size_t smem,
+                          cudaStream_t s) {
+    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_exact_kernel<NREP, G>), smem));
+    Q3_TRY_LAUNCH(launch(attn_scores_exact_kernel<NREP, G>, dim3(grid), dim3(sx_threads(G)), smem, s, 1, mk, a, pl));
+    return Q3_OK;
+}
+
 template <int NREP>
 int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
     ScoreXPlan pl;
@@ -1150,15 +1167,19 @@ int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
     pl.k_cols_per_head = a.kv.head >= a.kv.pos ? 0 : (int)a.kv.head;
     CUtensorMap mk;
     if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, SX_TILE)) return Q3_ERR_ARG;
-    const size_t base = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)SX_GROUPS * NREP * a.head_dim * 4 +
+    const int G = sx_groups(pl.halves);
+    if (pl.halves < 1 || pl.halves > 4 || SX_STAGES % (G * pl.halves) != 0) return Q3_ERR_SHAPE;
+    const size_t base = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)G * NREP * a.head_dim * 4 +
                         2 * SX_STAGES * 8 + (size_t)ITEM_TAB_OFF(a.B) * 4;
     pl.tab_cap = base < SMEM_CTA_MAX ? (int)std::min<size_t>(ITEM_TAB_MAX, (SMEM_CTA_MAX - base) / 8) : 0;
     const size_t smem = base + (size_t)pl.tab_cap * 8;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_scores_exact_kernel<NREP>), smem));
     const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + SX_TILE - 1) / SX_TILE);
     const int grid = (int)std::min<long long>(max_items, num_sms());
-    Q3_TRY_LAUNCH(launch(attn_scores_exact_kernel<NREP>, dim3(grid), dim3(SX_THREADS), smem, s, 1, mk, a, pl));
-    return Q3_OK;
+    switch (G) {
+        case 6: return launch_scores_exact_g<NREP, 6>(mk, a, pl, grid, smem, s);
+        case 4: return launch_scores_exact_g<NREP, 4>(mk, a, pl, grid, smem, s);
+        default: return launch_scores_exact_g<NREP, 3>(mk, a, pl, grid, smem, s);
+    }
 }
 
 // One block of 128 * NREP threads per (sequence, kv head).

@@ -112,9 +112,22 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16 *out, const bf16 *in,
 }
 
 // ------------------------------------------------------------------ qk_norm_rope
-// src/kernels.cu:301-403: one block of head_dim threads per q or k head (grid.x), one sequence
-// per grid.y. q/k/v strides are in elements between consecutive sequences; the cache row of
-// sequence b, position t, kv head h starts at key_cache + b*kv.seq + t*kv.pos + h*kv.head.
+// The per-head RMSNorm, RoPE and cache write of src/kernels.cu:301-403, one WARP per (sequence,
+// q or k head) instead of one head_dim-thread block: the reference's block of head_dim threads is
+// head_dim / 32 warps, and lane l here holds the elements l, l + 32, ... of the head -- element
+// l + 32*j is the reference's warp j, lane l. So the same arithmetic runs without a block barrier
+// or shared-memory exchange:
+//   - the sum of squares: per element x*x, one xor-shuffle tree per reference warp j (all lanes
+//     end with the bit-identical warp total), the totals added in j order from 0 -- the
+//     reference's warp_sums loop;
+//   - rsqrtf(total / head_dim + eps), then bf16(bf16(x * inv_rms) * w) per element;
+//   - RoPE pairs element t with t + head_dim/2. For head_dim a multiple of 64 both sit in the same
+//     lane (slots j and j + head_dim/64), so each lane rotates its own pairs in registers; other
+//     head widths exchange the normed head through the warp's slice of shared memory.
+// The rotation keeps the reference's rounding: c and s rounded to bf16, each product rounded,
+// then the difference and the sum. Eight heads share a 256-thread CTA. q/k/v strides are in
+// elements between consecutive sequences; the cache row of sequence b, position t, kv head h
+// starts at key_cache + b*kv.seq + t*kv.pos + h*kv.head.
 struct RopeArgs {
     bf16 *q, *k;
     const bf16 *v;
@@ -124,80 +137,122 @@ struct RopeArgs {
     bf16 *q_tap, *k_tap;
     long long q_stride, kv_stride;
     KvLayout kv;
-    int n_heads, head_dim;
+    int n_heads, n_kv_heads, head_dim, n_rows;
     int max_seq;  // > 0: positions are range-checked
     float eps, theta;
 };
 
-__global__ void __launch_bounds__(1024) qk_norm_rope_kernel(const __grid_constant__ RopeArgs a) {
+constexpr int ROPE_WARPS = 8;
+constexpr int ROPE_EPL = 32;  // elements per lane at the largest head_dim (1024)
+
+// EPL: elements per lane (head_dim / 32) when fixed at compile time -- then a pair's two
+// elements are registers j and j + EPL/2 of one lane -- or 0 for any head_dim, whose pairs meet
+// in shared memory.
+template <int EPL>
+__global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(const __grid_constant__ RopeArgs a) {
+    constexpr int NE = EPL > 0 ? EPL : ROPE_EPL;
+    constexpr bool REG_PAIRS = EPL > 0 && EPL % 2 == 0;
     pdl_trigger();
     pdl_wait();
-    const int b = blockIdx.y;
-    int head = blockIdx.x;
-    const int is_key = head >= a.n_heads;
+    const int lane = threadIdx.x % 32, wib = threadIdx.x / 32;
+    const long long gw = (long long)blockIdx.x * ROPE_WARPS + wib;
+    const int per_row = a.n_heads + a.n_kv_heads;
+    if (gw >= (long long)per_row * a.n_rows) return;
+    const int b = (int)(gw / per_row);
+    int head = (int)(gw % per_row);
+    const bool is_key = head >= a.n_heads;
+    const int D = EPL > 0 ? 32 * EPL : a.head_dim, epl = D / 32, half = D / 2;
     bf16 *x;
     const bf16 *norm_w;
     bf16 *tap;
     if (is_key) {
         head -= a.n_heads;
-        x = a.k + b * a.kv_stride + head * a.head_dim;
+        x = a.k + b * a.kv_stride + head * D;
         norm_w = a.k_norm_w;
-        tap = a.k_tap ? a.k_tap + b * a.kv_stride : nullptr;
+        tap = a.k_tap ? a.k_tap + b * a.kv_stride + head * D : nullptr;
     } else {
-        x = a.q + b * a.q_stride + head * a.head_dim;
+        x = a.q + b * a.q_stride + head * D;
         norm_w = a.q_norm_w;
-        tap = a.q_tap ? a.q_tap + b * a.q_stride : nullptr;
+        tap = a.q_tap ? a.q_tap + b * a.q_stride + head * D : nullptr;
     }
-    const int i = threadIdx.x;
     const int pos = a.pos[b];
     if (a.max_seq > 0 && (pos < 0 || pos >= a.max_seq)) {
-        if (i == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
+        if (lane == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
         return;
     }
 
-    const float xi = __bfloat162float(x[i]);
-    float sum = xi * xi;
-    for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-    __shared__ float warp_sums[32];
-    if (i % 32 == 0) warp_sums[i / 32] = sum;
-    __syncthreads();
+    float xv[NE];
     float total = 0.0f;
-    const int n_warps = blockDim.x / 32;
-    for (int w = 0; w < n_warps; w++) total += warp_sums[w];
-    const float inv_rms = rsqrtf(total / a.head_dim + a.eps);
-
-    const bf16 normed = __float2bfloat16(xi * inv_rms);
-    const bf16 y = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(norm_w[i]));
-    if (tap != nullptr) tap[head * a.head_dim + i] = y;
-
-    __shared__ bf16 normed_head[1024];
-    normed_head[i] = y;
-    __syncthreads();
-
-    const int half = a.head_dim / 2;
-    const size_t slot = (size_t)b * a.kv.seq + (size_t)pos * a.kv.pos + (size_t)head * a.kv.head;
-    if (i < half) {
-        const int j = i;
-        const float inv_freq = 1.0f / powf(a.theta, (float)(2 * j) / a.head_dim);
-        const float angle = pos * inv_freq;
-        const float c = round_bf16(cosf(angle));
-        const float s = round_bf16(sinf(angle));
-        const float av = __bfloat162float(normed_head[j]);
-        const float bv = __bfloat162float(normed_head[j + half]);
-        const float a_cos = round_bf16(av * c);
-        const float b_sin = round_bf16(bv * s);
-        const float b_cos = round_bf16(bv * c);
-        const float a_sin = round_bf16(av * s);
-        const bf16 out_a = __float2bfloat16(a_cos - b_sin);
-        const bf16 out_b = __float2bfloat16(b_cos + a_sin);
-        x[j] = out_a;
-        x[j + half] = out_b;
-        if (is_key) {
-            a.key_cache[slot + j] = out_a;
-            a.key_cache[slot + j + half] = out_b;
+#pragma unroll
+    for (int j = 0; j < NE; j++) {
+        if (j < epl) {
+            xv[j] = __bfloat162float(x[lane + 32 * j]);
+            // separate multiply and adds, as the reference's `sum = xi * xi; sum += shfl(...)`
+            // (no contraction into a fused multiply-add)
+            float sum = __fmul_rn(xv[j], xv[j]);
+            for (int off = 16; off > 0; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+            total = __fadd_rn(total, sum);
         }
     }
-    if (is_key) a.value_cache[slot + i] = a.v[b * a.kv_stride + head * a.head_dim + i];
+    const float inv_rms = rsqrtf(total / D + a.eps);
+    float y[NE];
+#pragma unroll
+    for (int j = 0; j < NE; j++) {
+        if (j < epl) {
+            const int t = lane + 32 * j;
+            const bf16 normed = __float2bfloat16(xv[j] * inv_rms);
+            const bf16 yb = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(norm_w[t]));
+            if (tap != nullptr) tap[t] = yb;
+            y[j] = __bfloat162float(yb);
+        }
+    }
+    bf16 *stage = nullptr;
+    if constexpr (!REG_PAIRS) {
+        __shared__ bf16 stage_s[ROPE_WARPS][1024];
+        stage = stage_s[wib];
+#pragma unroll
+        for (int j = 0; j < NE; j++)
+            if (j < epl) stage[lane + 32 * j] = __float2bfloat16(y[j]);
+        __syncwarp();
+    }
+
+    const size_t slot = (size_t)b * a.kv.seq + (size_t)pos * a.kv.pos + (size_t)head * a.kv.head;
+#pragma unroll
+    for (int j = 0; j < NE; j++) {
+        const int t = lane + 32 * j;  // the pair's first element
+        if (j < epl && t < half) {
+            const float inv_freq = 1.0f / powf(a.theta, (float)(2 * t) / D);
+            const float angle = pos * inv_freq;
+            const float c = round_bf16(cosf(angle));
+            const float s = round_bf16(sinf(angle));
+            float av, bv;
+            if constexpr (REG_PAIRS) {
+                av = y[j];
+                bv = y[(j + EPL / 2) % NE];  // j < EPL / 2 here
+            } else {
+                av = __bfloat162float(stage[t]);
+                bv = __bfloat162float(stage[t + half]);
+            }
+            const float a_cos = round_bf16(av * c);
+            const float b_sin = round_bf16(bv * s);
+            const float b_cos = round_bf16(bv * c);
+            const float a_sin = round_bf16(av * s);
+            const bf16 out_a = __float2bfloat16(a_cos - b_sin);
+            const bf16 out_b = __float2bfloat16(b_cos + a_sin);
+            x[t] = out_a;
+            x[t + half] = out_b;
+            if (is_key) {
+                a.key_cache[slot + t] = out_a;
+                a.key_cache[slot + t + half] = out_b;
+            }
+        }
+    }
+    if (is_key) {
+        const bf16 *vh = a.v + b * a.kv_stride + head * D;
+#pragma unroll
+        for (int j = 0; j < NE; j++)
+            if (j < epl) a.value_cache[slot + lane + 32 * j] = vh[lane + 32 * j];
+    }
 }
 
 // ------------------------------------------------------------------ argmax
@@ -442,11 +497,21 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
     a.kv_stride = kv_stride;
     a.kv = kv;
     a.n_heads = n_heads;
+    a.n_kv_heads = n_kv_heads;
     a.head_dim = head_dim;
+    a.n_rows = n_rows;
     a.max_seq = max_seq;
     a.eps = eps;
     a.theta = theta;
-    Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel, dim3(n_heads + n_kv_heads, n_rows), dim3(head_dim), 0, s, 1, a));
+    const long long warps = (long long)(n_heads + n_kv_heads) * n_rows;
+    if ((warps + ROPE_WARPS - 1) / ROPE_WARPS >= (1LL << 31)) return Q3_ERR_SHAPE;
+    const dim3 grid((unsigned)((warps + ROPE_WARPS - 1) / ROPE_WARPS)), block(ROPE_WARPS * 32);
+    switch (head_dim) {
+        case 64: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<2>, grid, block, 0, s, 1, a)); break;
+        case 128: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<4>, grid, block, 0, s, 1, a)); break;
+        case 256: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<8>, grid, block, 0, s, 1, a)); break;
+        default: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<0>, grid, block, 0, s, 1, a)); break;
+    }
     return Q3_OK;
 }
 

@@ -63,6 +63,32 @@ def test_dropin_kernel_vs_oracle(kind, name, p):
             assert np.array_equal(v, orc[k]), f"{k}: {v} vs {orc[k]}"
 
 
+# Head widths the fixtures do not cover: the warp-per-head kernel pairs RoPE elements in
+# registers when head_dim is a multiple of 64 (64, 128, 256 above) and through shared memory
+# otherwise. Compared with the reference's kernels run live (bit for bit) where oracle/_ref was
+# shipped, and with the CPU oracle within its libm tolerance in any case.
+@pytest.mark.parametrize("hd,pos", [(32, 5), (96, 1234), (192, 3000), (1024, 9)])
+def test_qk_norm_rope_any_head_width(hd, pos):
+    import ref_kernels
+    p = {"seed": 900 + hd, "n_heads": 6, "n_kv": 3, "hd": hd, "pos": pos, "max_seq": pos + 3}
+    inp = cases.inputs("qk_norm_rope", p)
+    mine = cases.run("mine", "qk_norm_rope", p, inp)
+    orc = cases.run("oracle", "qk_norm_rope", p, inp)
+    ref = cases.run("ref", "qk_norm_rope", p, inp) if ref_kernels.available() else None
+    max_ulp, max_frac = ORACLE_TOL["qk_norm_rope"]
+    for k, v in mine.items():
+        if ref is not None:
+            assert np.array_equal(v, ref[k]), f"{k}: differs from the reference kernels"
+        if v.dtype == np.uint16:
+            d = O.ulp_diff(v, orc[k])
+            # the libm allowance (host cosf / sinf / powf against CUDA's, last bit, which the bf16
+            # rounding rarely shows), but at least 1 % of these small heads' elements
+            assert d.max() <= max_ulp and np.count_nonzero(d) <= max(0.01 * d.size, max_frac * d.size), \
+                f"{k}: max {d.max()} ulp from the oracle"
+        else:
+            assert np.array_equal(v, orc[k]), k
+
+
 def _pkg():
     sys.path.insert(0, str(HERE))
     import conftest  # noqa: F401
