@@ -124,10 +124,12 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(bf16 *out, const bf16 *in,
 //   - RoPE pairs element t with t + head_dim/2. For head_dim a multiple of 64 both sit in the same
 //     lane (slots j and j + head_dim/64), so each lane rotates its own pairs in registers; other
 //     head widths exchange the normed head through the warp's slice of shared memory.
-// The rotation keeps the reference's rounding: c and s rounded to bf16, each product rounded,
-// then the difference and the sum. Eight heads share a 256-thread CTA. q/k/v strides are in
-// elements between consecutive sequences; the cache row of sequence b, position t, kv head h
-// starts at key_cache + b*kv.seq + t*kv.pos + h*kv.head.
+// The rotation angle depends on the position and the pair only, so a CTA -- one sequence's block
+// of eight heads -- computes the rounded cos / sin of each pair once, before its warps start
+// (the reference computes them per head; the values are the same). Each product keeps the
+// reference's rounding: c and s rounded to bf16, each product rounded, then the difference and
+// the sum. q/k/v strides are in elements between consecutive sequences; the cache row of sequence
+// b, position t, kv head h starts at key_cache + b*kv.seq + t*kv.pos + h*kv.head.
 struct RopeArgs {
     bf16 *q, *k;
     const bf16 *v;
@@ -137,31 +139,42 @@ struct RopeArgs {
     bf16 *q_tap, *k_tap;
     long long q_stride, kv_stride;
     KvLayout kv;
-    int n_heads, n_kv_heads, head_dim, n_rows;
+    int n_heads, n_kv_heads, head_dim;
     int max_seq;  // > 0: positions are range-checked
     float eps, theta;
 };
 
-constexpr int ROPE_WARPS = 8;
-constexpr int ROPE_EPL = 32;  // elements per lane at the largest head_dim (1024)
+constexpr int ROPE_WARPS = 8;  // heads per CTA
+constexpr int ROPE_EPL = 32;   // elements per lane at the largest head_dim (1024)
 
 // EPL: elements per lane (head_dim / 32) when fixed at compile time -- then a pair's two
 // elements are registers j and j + EPL/2 of one lane -- or 0 for any head_dim, whose pairs meet
-// in shared memory.
+// in shared memory. Grid: (head blocks of ROPE_WARPS, sequences).
 template <int EPL>
 __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(const __grid_constant__ RopeArgs a) {
     constexpr int NE = EPL > 0 ? EPL : ROPE_EPL;
     constexpr bool REG_PAIRS = EPL > 0 && EPL % 2 == 0;
+    __shared__ float cs_s[512], sn_s[512];  // rounded cos / sin of each pair at this position
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x % 32, wib = threadIdx.x / 32;
-    const long long gw = (long long)blockIdx.x * ROPE_WARPS + wib;
-    const int per_row = a.n_heads + a.n_kv_heads;
-    if (gw >= (long long)per_row * a.n_rows) return;
-    const int b = (int)(gw / per_row);
-    int head = (int)(gw % per_row);
-    const bool is_key = head >= a.n_heads;
+    const int b = blockIdx.y;
     const int D = EPL > 0 ? 32 * EPL : a.head_dim, epl = D / 32, half = D / 2;
+    const int pos = a.pos[b];
+    if (a.max_seq > 0 && (pos < 0 || pos >= a.max_seq)) {  // uniform over the CTA
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
+        return;
+    }
+    for (int t = threadIdx.x; t < half; t += ROPE_WARPS * 32) {  // src/kernels.cu:359-365
+        const float inv_freq = 1.0f / powf(a.theta, (float)(2 * t) / D);
+        const float angle = pos * inv_freq;
+        cs_s[t] = round_bf16(cosf(angle));
+        sn_s[t] = round_bf16(sinf(angle));
+    }
+    __syncthreads();
+    int head = blockIdx.x * ROPE_WARPS + wib;
+    if (head >= a.n_heads + a.n_kv_heads) return;
+    const bool is_key = head >= a.n_heads;
     bf16 *x;
     const bf16 *norm_w;
     bf16 *tap;
@@ -175,18 +188,15 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(const __g
         norm_w = a.q_norm_w;
         tap = a.q_tap ? a.q_tap + b * a.q_stride + head * D : nullptr;
     }
-    const int pos = a.pos[b];
-    if (a.max_seq > 0 && (pos < 0 || pos >= a.max_seq)) {
-        if (lane == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
-        return;
-    }
 
     float xv[NE];
+#pragma unroll
+    for (int j = 0; j < NE; j++)
+        if (j < epl) xv[j] = __bfloat162float(x[lane + 32 * j]);
     float total = 0.0f;
 #pragma unroll
     for (int j = 0; j < NE; j++) {
         if (j < epl) {
-            xv[j] = __bfloat162float(x[lane + 32 * j]);
             // separate multiply and adds, as the reference's `sum = xi * xi; sum += shfl(...)`
             // (no contraction into a fused multiply-add)
             float sum = __fmul_rn(xv[j], xv[j]);
@@ -221,10 +231,7 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(const __g
     for (int j = 0; j < NE; j++) {
         const int t = lane + 32 * j;  // the pair's first element
         if (j < epl && t < half) {
-            const float inv_freq = 1.0f / powf(a.theta, (float)(2 * t) / D);
-            const float angle = pos * inv_freq;
-            const float c = round_bf16(cosf(angle));
-            const float s = round_bf16(sinf(angle));
+            const float c = cs_s[t], sn = sn_s[t];
             float av, bv;
             if constexpr (REG_PAIRS) {
                 av = y[j];
@@ -234,9 +241,9 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(const __g
                 bv = __bfloat162float(stage[t + half]);
             }
             const float a_cos = round_bf16(av * c);
-            const float b_sin = round_bf16(bv * s);
+            const float b_sin = round_bf16(bv * sn);
             const float b_cos = round_bf16(bv * c);
-            const float a_sin = round_bf16(av * s);
+            const float a_sin = round_bf16(av * sn);
             const bf16 out_a = __float2bfloat16(a_cos - b_sin);
             const bf16 out_b = __float2bfloat16(b_cos + a_sin);
             x[t] = out_a;
@@ -499,13 +506,12 @@ int qk_norm_rope(bf16 *q, bf16 *k, const bf16 *v, const bf16 *q_norm_w, const bf
     a.n_heads = n_heads;
     a.n_kv_heads = n_kv_heads;
     a.head_dim = head_dim;
-    a.n_rows = n_rows;
     a.max_seq = max_seq;
     a.eps = eps;
     a.theta = theta;
-    const long long warps = (long long)(n_heads + n_kv_heads) * n_rows;
-    if ((warps + ROPE_WARPS - 1) / ROPE_WARPS >= (1LL << 31)) return Q3_ERR_SHAPE;
-    const dim3 grid((unsigned)((warps + ROPE_WARPS - 1) / ROPE_WARPS)), block(ROPE_WARPS * 32);
+    if (n_rows > 65535) return Q3_ERR_SHAPE;  // grid.y
+    const dim3 grid((unsigned)((n_heads + n_kv_heads + ROPE_WARPS - 1) / ROPE_WARPS), (unsigned)n_rows),
+        block(ROPE_WARPS * 32);
     switch (head_dim) {
         case 64: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<2>, grid, block, 0, s, 1, a)); break;
         case 128: Q3_TRY_LAUNCH(launch(qk_norm_rope_kernel<4>, grid, block, 0, s, 1, a)); break;
