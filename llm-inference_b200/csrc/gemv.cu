@@ -17,13 +17,21 @@
 // never depend on the previous kernel, and the next row's first batch is loaded before the
 // current row's reduction and store. x is read through L1, where every warp of the SM finds it.
 //
+// The input vector x is the previous launch's output. After the programmatic-dependency wait every
+// CTA copies it into shared memory with cp.async, all of its 16-byte pieces in flight at once (one
+// round trip to L2), and the dot products read it from there: read from global memory inside the
+// dot loop, its loads serialized behind the register-bound weight batch, it cost the residual
+// projections about half their time in a decode step (o_proj 7.7 us and down 15.9 us per layer
+// after the wait at batch 1, against rooflines of 3.2 and 7.6). Vectors wider than GV_X_MAX_COLS
+// stay in global memory.
+//
 // Fused RMSNorm (NORM): when the projection's input is rmsnorm(x) (qkv, gate_up and the LM head
 // take the normed residual stream), every CTA recomputes the normed vector itself into shared
 // memory, with the reference rmsnorm_kernel's arithmetic (src/kernels.cu:25-71: 256 threads,
 // thread t summing x[t], x[t + 256], ... with fused multiply-adds, an xor tree per warp, the eight
-// warp sums in order, then bf16(bf16(x * inv_rms) * w)); the norm weight is staged before the
-// programmatic-dependency wait. The separate rmsnorm launch and its dependency hop disappear; the
-// extra reads (x and the weight, a few KB per CTA) come from L2.
+// warp sums in order, then bf16(bf16(x * inv_rms) * w)), from the staged copy of x; the norm weight
+// is staged before the programmatic-dependency wait. The separate rmsnorm launch and its
+// dependency hop disappear; the extra reads (x and the weight, a few KB per CTA) come from L2.
 #include <algorithm>
 
 #include "common.cuh"
@@ -59,7 +67,15 @@ struct GemvArgs {
     float eps;
 };
 
-constexpr int GV_NORM_MAX_COLS = 8192;  // NORM: the normed vector lives in shared memory
+constexpr int GV_NORM_MAX_COLS = 8192;   // NORM: the weight and x, then the normed x, in shared memory
+constexpr int GV_X_MAX_COLS = 16384;     // x staged in shared memory up to this width
+
+// How a kernel reads its input vector.
+enum XMode : int { X_GLOBAL = 0, X_STAGED = 1, X_NORM = 2 };
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
 
 template <int EPI>
 __device__ __forceinline__ const bf16 *unit_row(const GemvArgs &a, int u, int r) {
@@ -82,13 +98,15 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p, uint64_t policy) {
     return v;
 }
 
-template <int EPI, int UR, bool NORM, int THREADS, int MINB>
+template <int EPI, int UR, int XMODE, int THREADS, int MINB>
 __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_constant__ GemvArgs a) {
+    constexpr bool NORM = XMODE == X_NORM;
     constexpr int REF = 256;                      // the reference rmsnorm's block
     constexpr int NREF = REF / THREADS;           // reference threads each thread stands in for
     static_assert(REF % THREADS == 0, "the rmsnorm order needs a divisor of 256 threads");
     constexpr int RPU = EPI == GATE_UP ? 2 : 1;  // weight rows per output unit
-    extern __shared__ __align__(16) bf16 xs[];    // NORM: [cols], the norm weight, then the normed x
+    // X_STAGED: [cols] x; NORM: [cols] the norm weight, then the normed x, and [cols] x
+    extern __shared__ __align__(16) bf16 xs[];
     __shared__ float warp_sums[REF / 32];
     const int lane = threadIdx.x % 32;
     const int nw = gridDim.x * (THREADS / 32);
@@ -114,6 +132,13 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
     if (NORM)
         for (int i = threadIdx.x; i < a.cols; i += THREADS) xs[i] = a.norm_w[i];
     pdl_wait();
+    bf16 *xraw = NORM ? xs + a.cols : xs;  // the staged x
+    if (XMODE != X_GLOBAL) {
+        const uint4 *xg = reinterpret_cast<const uint4 *>(a.x);
+        for (int i = threadIdx.x; i < n_vec; i += THREADS) cp_async16(reinterpret_cast<uint4 *>(xraw) + i, xg + i);
+        asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+    }
     if (NORM) {
         // reference thread r = threadIdx.x + k * THREADS sums x[r], x[r + 256], ... (accumulator k)
         float sum[NREF];
@@ -124,7 +149,7 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
             for (int k = 0; k < NREF; k++) {
                 const int i = i0 + threadIdx.x + k * THREADS;
                 if (i < a.cols) {
-                    const float v = __bfloat162float(a.x[i]);
+                    const float v = __bfloat162float(xraw[i]);
                     sum[k] = __fmaf_rn(v, v, sum[k]);
                 }
             }
@@ -139,12 +164,12 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
         for (int w_ = 0; w_ < REF / 32; w_++) total += warp_sums[w_];
         const float inv_rms = rsqrtf(total / a.cols + a.eps);
         for (int i = threadIdx.x; i < a.cols; i += THREADS) {  // each thread rewrites its own elements
-            const bf16 normed = __float2bfloat16(__bfloat162float(a.x[i]) * inv_rms);
+            const bf16 normed = __float2bfloat16(__bfloat162float(xraw[i]) * inv_rms);
             xs[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(xs[i]));
         }
         __syncthreads();
     }
-    const uint4 *xv = reinterpret_cast<const uint4 *>(NORM ? xs : a.x);
+    const uint4 *xv = reinterpret_cast<const uint4 *>(XMODE == X_GLOBAL ? a.x : xs);
     for (; u < a.units; u += nw) {
         float acc[RPU];
 #pragma unroll
@@ -155,7 +180,7 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
             for (int j = 0; j < UR; j++) {
                 const int i = lane + 32 * (r0 + j);
                 if (i < n_vec) {
-                    const bf16x8 xc = NORM ? lds128(xv + i) : ldg128(xv + i);
+                    const bf16x8 xc = XMODE == X_GLOBAL ? ldg128(xv + i) : lds128(xv + i);
 #pragma unroll
                     for (int r = 0; r < RPU; r++) acc[r] = dot8(*reinterpret_cast<const bf16x8 *>(&w[r][j]), xc, acc[r]);
                 }
@@ -194,18 +219,22 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
 
 bool aligned16(const void *p) { return p == nullptr || (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-template <int EPI, int UR, bool NORM, int MINB = 1>
-int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
+template <int EPI, int UR, int XMODE, int MINB = 1>
+int launch_gemv_x(const GemvArgs &a, cudaStream_t stream) {
     constexpr int THREADS = EPI == RESIDUAL ? GV_THREADS_RESIDUAL : GV_THREADS;
     static int per_sm[64] = {};  // resident CTAs per SM, by device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return Q3_ERR_DEVICE;
-    // NORM: occupancy counted at the largest normed vector, so one grid size fits every width
-    const size_t smem = NORM ? (size_t)a.cols * 2 : 0, smem_plan = NORM ? (size_t)GV_NORM_MAX_COLS * 2 : 0;
+    // occupancy counted at the largest staged vector, so one grid size fits every width
+    const size_t smem = XMODE == X_NORM ? (size_t)a.cols * 4 : XMODE == X_STAGED ? (size_t)a.cols * 2 : 0;
+    const size_t smem_plan = XMODE == X_NORM     ? (size_t)GV_NORM_MAX_COLS * 4
+                             : XMODE == X_STAGED ? (size_t)GV_X_MAX_COLS * 2
+                                                 : 0;
     if (per_sm[dev] == 0) {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(gemv_kernel<EPI, UR, XMODE, THREADS, MINB>), smem_plan));
         int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, NORM, THREADS, MINB>, THREADS,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_kernel<EPI, UR, XMODE, THREADS, MINB>, THREADS,
                                                           smem_plan) !=
                 cudaSuccess ||
             n < 1)
@@ -215,13 +244,15 @@ int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
     }
     const long long want = (a.units + THREADS / 32 - 1) / (THREADS / 32);
     const int grid = (int)std::min<long long>(want, (long long)num_sms() * per_sm[dev]);
-    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, NORM, THREADS, MINB>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
+    Q3_TRY_LAUNCH(launch(gemv_kernel<EPI, UR, XMODE, THREADS, MINB>, dim3(grid), dim3(THREADS), smem, stream, 1, a));
     return Q3_OK;
 }
 
-template <int EPI, int UR>
+template <int EPI, int UR, int MINB = 1>
 int launch_gemv_ur(const GemvArgs &a, cudaStream_t stream) {
-    return a.norm_w ? launch_gemv_ur<EPI, UR, true>(a, stream) : launch_gemv_ur<EPI, UR, false>(a, stream);
+    if (a.norm_w) return launch_gemv_x<EPI, UR, X_NORM, MINB>(a, stream);
+    if (a.cols <= GV_X_MAX_COLS) return launch_gemv_x<EPI, UR, X_STAGED, MINB>(a, stream);
+    return launch_gemv_x<EPI, UR, X_GLOBAL, MINB>(a, stream);
 }
 
 template <int EPI>
@@ -236,11 +267,11 @@ int launch_gemv(GemvArgs a, cudaStream_t stream) {
     if (rounds <= 10) return launch_gemv_ur<EPI, 10>(a, stream);
     if (rounds <= 12) return launch_gemv_ur<EPI, 12>(a, stream);
     if constexpr (EPI == RESIDUAL) {
-        if (rounds <= 16) return launch_gemv_ur<EPI, 16, false, 5>(a, stream);
+        if (rounds <= 16) return launch_gemv_ur<EPI, 16, 5>(a, stream);
 #if Q3_GEMV_LONG_ROWS
         // long rows (down_proj: 38 rounds): 20 chunks per lane in flight, two batches a row instead
         // of three; at most 102 registers keep 5 CTAs (20 warps) per SM, one row per warp
-        if (rounds <= 40) return launch_gemv_ur<EPI, 20, false, 5>(a, stream);
+        if (rounds <= 40) return launch_gemv_ur<EPI, 20, 5>(a, stream);
 #endif
     }
     if constexpr (EPI == GATE_UP) {
