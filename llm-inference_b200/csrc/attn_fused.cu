@@ -103,6 +103,12 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     __shared__ float cm_s[FA_MAX_CLUSTER * NREP];
     __shared__ float gmax_s[NREP], gsum_s[NREP];
     __shared__ float chs[NREP * FA_TILE];  // sums of the chains this CTA computes (per_cta <= NREP * 128)
+    // RoPE: each pair's inverse frequency, then its rounded cos and sin at this position. The
+    // reference computes them per head (src/kernels.cu:359-365); the NREP + 1 heads of the group
+    // share one computation here (the values are the same), the frequencies before the
+    // programmatic-dependency wait.
+    constexpr int HALF = HD / 2;
+    __shared__ float rope_f[HALF], rope_c[HALF], rope_s[HALF];
 
     cg::cluster_group cluster = cg::this_cluster();
     const int tid = threadIdx.x, lane = tid % 32;
@@ -117,6 +123,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         prefetch_tmap(&tmK);
         prefetch_tmap(&tmV);
     }
+    for (int j = tid; j < HALF; j += FA_THREADS) rope_f[j] = 1.0f / powf(a.theta, (float)(2 * j) / HD);
     __syncthreads();
     pdl_trigger();  // no CTA here waits for another grid's CTAs: successors may be scheduled early
     pdl_wait();
@@ -138,6 +145,11 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         return;
     }
     const int len = p + 1;
+    for (int j = tid; j < HALF; j += FA_THREADS) {  // ordered before the RoPE by the norm's barriers
+        const float angle = p * rope_f[j];
+        rope_c[j] = round_bf16(cosf(angle));
+        rope_s[j] = round_bf16(sinf(angle));
+    }
     const int CH = (len + C - 1) / C;  // positions per chunk (<= cap)
     const int t0 = min(len, c * CH), t1 = min(len, t0 + CH);
     const int n_own = t1 - t0;
@@ -201,13 +213,9 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     }
     __syncthreads();
     // RoPE at position p (src/kernels.cu:349-390): pairs (j, j + HD/2)
-    constexpr int HALF = HD / 2;
     for (int e = tid; e < (NREP + 1) * HALF; e += FA_THREADS) {
         const int hh = e / HALF, j = e % HALF;
-        const float inv_freq = 1.0f / powf(a.theta, (float)(2 * j) / HD);
-        const float angle = p * inv_freq;
-        const float cs = round_bf16(cosf(angle));
-        const float sn = round_bf16(sinf(angle));
+        const float cs = rope_c[j], sn = rope_s[j];
         const float av = __bfloat162float(yh[hh * HD + j]);
         const float bv = __bfloat162float(yh[hh * HD + j + HALF]);
         const bf16 out_a = __float2bfloat16(round_bf16(av * cs) - round_bf16(bv * sn));

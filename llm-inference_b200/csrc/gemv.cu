@@ -144,6 +144,7 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
         float sum[NREF];
 #pragma unroll
         for (int k = 0; k < NREF; k++) sum[k] = 0.0f;
+#pragma unroll 8
         for (int i0 = 0; i0 < a.cols; i0 += REF)
 #pragma unroll
             for (int k = 0; k < NREF; k++) {
@@ -163,9 +164,18 @@ __global__ void __launch_bounds__(THREADS, MINB) gemv_kernel(const __grid_consta
 #pragma unroll
         for (int w_ = 0; w_ < REF / 32; w_++) total += warp_sums[w_];
         const float inv_rms = rsqrtf(total / a.cols + a.eps);
-        for (int i = threadIdx.x; i < a.cols; i += THREADS) {  // each thread rewrites its own elements
-            const bf16 normed = __float2bfloat16(__bfloat162float(xraw[i]) * inv_rms);
-            xs[i] = __float2bfloat16(__bfloat162float(normed) * __bfloat162float(xs[i]));
+        // bf16(bf16(x * inv_rms) * w), eight elements per thread and step (an element's value does not
+        // depend on which thread computes it)
+        for (int c = threadIdx.x; c < n_vec; c += THREADS) {
+            const bf16x8 xr = lds128(xraw + 8 * c), wr = lds128(xs + 8 * c);
+            bf16x8 o;
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float2 xf = __bfloat1622float2(xr.h[e]), wf = __bfloat1622float2(wr.h[e]);
+                const float n0 = round_bf16(xf.x * inv_rms), n1 = round_bf16(xf.y * inv_rms);
+                o.h[e] = __floats2bfloat162_rn(n0 * wf.x, n1 * wf.y);
+            }
+            *reinterpret_cast<bf16x8 *>(xs + 8 * c) = o;
         }
         __syncthreads();
     }
