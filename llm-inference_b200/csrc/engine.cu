@@ -273,6 +273,11 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->pf_pos, B * 4);
     if (!mk && !(flags & (Q3_ENGINE_EXACT_ATTENTION | Q3_ENGINE_SPLIT_ATTENTION)))
         e->fused_chunks = fused_chunks(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq);
+    // With a thousand positions or more per cluster CTA the split-KV kernels, which spread every
+    // row over all SMs, are the faster path (measured on B200: Qwen3-1.7B, 8 sequences at position
+    // 2048, two-CTA clusters: 3544 tok/s fused, 3698 split; with a few hundred positions per CTA the
+    // fused launch wins, e.g. Qwen3-4B batch 1 at position 2048: 413 against 357).
+    if (e->fused_chunks > 0 && max_seq / e->fused_chunks >= 1024) e->fused_chunks = 0;
     if (mk) {
         e->mk = true;
         DsParams &p = e->mkp;
