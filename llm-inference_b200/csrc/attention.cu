@@ -112,6 +112,33 @@ struct Item {
     int b, kvh, c, nc, len;
 };
 
+// build_prefix over groups of G consecutive rows (the rows of one prompt, sharing a cache): a
+// group's length is its longest row's. G == 1 is build_prefix.
+__device__ int build_prefix_rows(const AttnArgs &a, int chunk, int *prefix, int G) {
+    const int Bg = (a.B + G - 1) / G;
+    int *lens = prefix + Bg + 1;
+    for (int g = threadIdx.x; g < Bg; g += blockDim.x) {
+        int n = 0;
+        for (int i = 0; i < G && g * G + i < a.B; i++) {
+            const int l = seq_len(a, g * G + i);
+            if (l == 0 && blockIdx.x == 0) atomicOr(&g_dev_error, DEV_ERR_POS_RANGE);
+            n = max(n, l);
+        }
+        lens[g] = n;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int total = 0;
+        for (int g = 0; g < Bg; g++) {
+            prefix[g] = total;
+            total += a.n_kv * ((lens[g] + chunk - 1) / chunk);
+        }
+        prefix[Bg] = total;
+    }
+    __syncthreads();
+    return prefix[Bg];
+}
+
 __device__ __forceinline__ Item find_item(const AttnArgs &a, const int *prefix, int chunk, int item) {
     Item it;
     int b = 0;
@@ -768,16 +795,17 @@ constexpr int PV_THREADS = 64 + PV_P_THREADS;  // producer warp, MMA warp, p war
 constexpr int PV_V_BYTES = PV_TILE * 128;      // one 64-dim half of a V tile
 constexpr int PV_P_OFF = 2 * PV_V_BYTES;       // P: 2 swizzle atoms of 16 rows x 128 B
 constexpr int PV_S_OFF = PV_P_OFF + 2 * 16 * 128;
-constexpr int PV_T_OFF = PV_S_OFF + 8 * PV_TILE * 4;        // scores of up to 8 heads
-constexpr int PV_STAGE_BYTES = PV_T_OFF + 1024;             // the group's (max, sum) pairs
+constexpr int PV_T_OFF = PV_S_OFF + 16 * PV_TILE * 4;       // scores of the 16 P rows
+constexpr int PV_STAGE_BYTES = PV_T_OFF + 1024;             // their (max, sum) pairs, 64 B per row
 
 struct PvTcPlan {
     int k_rows_per_seq, k_rows_per_head, k_cols_per_head;
     uint32_t idesc;
     int tab_cap;  // items the shared-memory item table holds
+    int rows;     // rows per item: 16 / NREP when the rows share one cache (a prompt), else 1
 };
 
-template <int NREP>
+template <int NREP, int GR>
 __global__ void __launch_bounds__(PV_THREADS, 1)
     attn_pv_tc_kernel(const __grid_constant__ CUtensorMap tmV, const __grid_constant__ AttnArgs a,
                       const __grid_constant__ PvTcPlan pl) {
@@ -806,11 +834,11 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         fence_barrier_init();
         prefetch_tmap(&tmV);
     }
-    if (warp >= 2) {  // zero the padding rows NREP..15 of every stage's P once
+    if (warp >= 2) {  // zero the padding rows (past rows x NREP) of every stage's P once
         const int t = threadIdx.x - 64;
         for (int j = t; j < PV_STAGES * 2 * 16 * 8; j += PV_P_THREADS) {  // 16-byte units
             const int st = j / 256, r = j % 256, atom = r / 128, row = (r % 128) / 8, c = r % 8;
-            if (row >= NREP)
+            if (row >= GR * NREP)
                 *reinterpret_cast<uint4 *>(smem + (size_t)st * PV_STAGE_BYTES + PV_P_OFF + atom * 2048 + row * 128 + c * 16) =
                     make_uint4(0, 0, 0, 0);
         }
@@ -827,28 +855,38 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
     const uint32_t tmem_base = *tmem_slot;
     pdl_trigger();
     pdl_wait();  // positions, scores and statistics come from the previous kernels
-    const int total = build_prefix(a, chunk, prefix);
+    // An item is (row group g, kv head, chunk): G rows r = g*G + i share the item's V tiles, and
+    // the MMA's N = 16 columns are their NREP heads each (G = 16 / NREP rows of one prompt, whose
+    // rows read one cache; one row otherwise). `ag` describes the groups to the item helpers.
+    constexpr int G = GR;
+    AttnArgs ag = a;
+    ag.B = (a.B + G - 1) / G;
+    const int total = build_prefix_rows(a, chunk, prefix, G);
     const int i0 = (int)((long long)total * blockIdx.x / gridDim.x);
     const int i1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
     int2 *tab = reinterpret_cast<int2 *>(prefix + ITEM_TAB_OFF(a.B));
-    const bool tabbed = fill_items(a, prefix, chunk, i0, i1 - i0, tab, pl.tab_cap);
-    int cur = i1 > i0 ? first_seq(prefix, a.B, i0) : 0;
+    const bool tabbed = fill_items(ag, prefix, chunk, i0, i1 - i0, tab, pl.tab_cap);
+    int cur = i1 > i0 ? first_seq(prefix, ag.B, i0) : 0;
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer: V tile halves by TMA, the group's scores by bulk copy
         const uint64_t stream_pol = policy_evict_first();  // V rows are read once per step
         int k = 0;
         bool ok = true;
+        const uint32_t stat_slot = 1024u / (uint32_t)G;  // bytes of the stats area per row
         for (int item = i0; item < i1 && ok; item++) {
-            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
+            const Item it = item_k(ag, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
-            const float *sc = a.scores + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
+            const int r0 = it.b * G, nr = min(G, a.B - r0);  // the item's rows
             const int row0 = it.b * pl.k_rows_per_seq + it.kvh * pl.k_rows_per_head;
-            // the group's statistics, from the 16-byte boundary below them (the stats region is
+            // each row's statistics, from the 16-byte boundary below them (the stats region is
             // padded to 256 bytes, so the rounded-up copy stays inside it)
-            const float *stp = a.stats + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * 2;
-            const uintptr_t st_al = reinterpret_cast<uintptr_t>(stp) & ~uintptr_t(15);
-            const uint32_t tbytes = (uint32_t)((reinterpret_cast<uintptr_t>(stp) - st_al + NREP * 8 + 15) & ~15u);
+            uint32_t tbytes_all = 0;
+            for (int i = 0; i < nr; i++) {
+                const float *stp = a.stats + ((size_t)(r0 + i) * a.n_heads + (size_t)it.kvh * NREP) * 2;
+                const uintptr_t st_al = reinterpret_cast<uintptr_t>(stp) & ~uintptr_t(15);
+                tbytes_all += (uint32_t)((reinterpret_cast<uintptr_t>(stp) - st_al + NREP * 8 + 15) & ~15u);
+            }
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
                 const int st = k % PV_STAGES;
                 if (k >= PV_STAGES && !mbar_wait(&empty[st], ((k / PV_STAGES) - 1) & 1, &g_dev_error)) {
@@ -859,13 +897,23 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
                 const uint32_t sbytes = (uint32_t)((rows + 3) / 4) * 16;  // within ld: ld is a multiple of 4
                 unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
                 const bool first = tt == t0;
-                mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + NREP * sbytes + (first ? tbytes : 0));
-                if (first) bulk_g2s(base + PV_T_OFF, reinterpret_cast<const void *>(st_al), tbytes, &full[st]);
+                mbar_arrive_expect_tx(&full[st], 2 * PV_V_BYTES + (uint32_t)(nr * NREP) * sbytes + (first ? tbytes_all : 0));
+                if (first)
+                    for (int i = 0; i < nr; i++) {
+                        const float *stp = a.stats + ((size_t)(r0 + i) * a.n_heads + (size_t)it.kvh * NREP) * 2;
+                        const uintptr_t st_al = reinterpret_cast<uintptr_t>(stp) & ~uintptr_t(15);
+                        const uint32_t tb = (uint32_t)((reinterpret_cast<uintptr_t>(stp) - st_al + NREP * 8 + 15) & ~15u);
+                        bulk_g2s(base + PV_T_OFF + i * stat_slot, reinterpret_cast<const void *>(st_al), tb, &full[st]);
+                    }
                 tma_load_2d_stream(base, &tmV, it.kvh * pl.k_cols_per_head, row0 + tt, &full[st], stream_pol);
                 tma_load_2d_stream(base + PV_V_BYTES, &tmV, it.kvh * pl.k_cols_per_head + TMA_BK, row0 + tt, &full[st], stream_pol);
+                for (int i = 0; i < nr; i++) {
+                    const float *sc = a.scores + ((size_t)(r0 + i) * a.n_heads + (size_t)it.kvh * NREP) * a.ld;
 #pragma unroll
-                for (int h = 0; h < NREP; h++)
-                    bulk_g2s(base + PV_S_OFF + h * PV_TILE * 4, sc + (size_t)h * a.ld + tt, sbytes, &full[st]);
+                    for (int h = 0; h < NREP; h++)
+                        bulk_g2s(base + PV_S_OFF + (i * NREP + h) * PV_TILE * 4, sc + (size_t)h * a.ld + tt, sbytes,
+                                 &full[st]);
+                }
             }
         }
         // drain: every issued copy lands before the CTA exits
@@ -880,7 +928,7 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
+            const Item it = item_k(ag, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
             const int buf = n_items % PV_ACC;
             if (n_items >= PV_ACC && !mbar_wait(&acc_empty[buf], ((n_items / PV_ACC) - 1) & 1, &g_dev_error)) break;
@@ -915,27 +963,36 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         // the MMA, so that waiting for the accumulator overlaps the next item's work.
         Item pend = {};
         int pend_n = -1;
+        // P rows n = i * NREP + h: row r0 + i of the item, query head h of the kv group
+        constexpr int NP = G * NREP;
+        const uint32_t stat_slot = 1024u / (uint32_t)G;
         auto epilogue = [&](const Item &it, int n_item) -> bool {
             const int buf = n_item % PV_ACC;
             // warp-uniform exit: tcgen05.ld below is warp-collective
             if (!__all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (n_item / PV_ACC) & 1, &g_dev_error))) return false;
             tc_fence_after();
-            float acc[8];
+            float acc[16];
             tmem_ld8(lane_addr + buf * 16, acc);
+            if (NP > 8) tmem_ld8(lane_addr + buf * 16 + 8, acc + 8);
             tmem_wait_ld();
             tc_fence_before();
             mbar_arrive(&acc_empty[buf]);
             if (d < a.head_dim) {
-                if (it.nc == 1) {
-                    bf16 *o = a.out + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * a.head_dim + d;
+                const int r0 = it.b * G;
 #pragma unroll
-                    for (int h = 0; h < NREP; h++)
-                        if (h % PV_GROUPS == grp) o[(size_t)h * a.head_dim] = __float2bfloat16(acc[h]);
-                } else {
-                    float *part = a.partial + ((size_t)it.b * a.n_heads + it.kvh * NREP) * a.max_chunks * a.head_dim;
-#pragma unroll
-                    for (int h = 0; h < NREP; h++)
-                        if (h % PV_GROUPS == grp) part[((size_t)h * a.max_chunks + it.c) * a.head_dim + d] = acc[h];
+                for (int n = 0; n < NP; n++) {
+                    if (n % PV_GROUPS != grp) continue;
+                    const int r = r0 + n / NREP, h = n % NREP;
+                    if (r >= a.B) continue;
+                    // this row's own chunk count: rows of a group end at different positions
+                    const int nc = G == 1 ? it.nc : (seq_len(a, r) + chunk - 1) / chunk;
+                    if (it.c >= nc) continue;
+                    if (nc == 1) {
+                        a.out[(size_t)r * a.q_stride + ((size_t)it.kvh * NREP + h) * a.head_dim + d] = __float2bfloat16(acc[n]);
+                    } else {
+                        float *part = a.partial + ((size_t)r * a.n_heads + it.kvh * NREP + h) * a.max_chunks * a.head_dim;
+                        part[(size_t)it.c * a.head_dim + d] = acc[n];
+                    }
                 }
             }
             return true;
@@ -943,9 +1000,13 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
         int k = 0, n_items = 0;
         bool ok = true;
         for (int item = i0; item < i1 && ok; item++, n_items++) {
-            const Item it = item_k(a, prefix, chunk, tab, tabbed, i0, item - i0, cur);
+            const Item it = item_k(ag, prefix, chunk, tab, tabbed, i0, item - i0, cur);
             const int t0 = it.c * chunk, t1 = min(t0 + chunk, it.len);
-            float m[NREP], sum[NREP];
+            const int r0 = it.b * G;
+            float m[NP], sum[NP];
+            int len[NP];  // each P row's sequence length: its positions past it get p = 0
+#pragma unroll
+            for (int n = 0; n < NP; n++) len[n] = G == 1 ? it.len : r0 + n / NREP < a.B ? seq_len(a, r0 + n / NREP) : 0;
             for (int tt = t0; tt < t1; tt += PV_TILE, k++) {
                 const int st = k % PV_STAGES;
                 if (!__all_sync(0xffffffffu, mbar_wait(&full[st], (k / PV_STAGES) & 1, &g_dev_error))) {
@@ -954,12 +1015,15 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
                 }
                 unsigned char *base = smem + (size_t)st * PV_STAGE_BYTES;
                 if (tt == t0) {  // the statistics came with the item's first tile
-                    const uintptr_t src = reinterpret_cast<uintptr_t>(a.stats + ((size_t)it.b * a.n_heads + (size_t)it.kvh * NREP) * 2);
-                    const float *stp = reinterpret_cast<const float *>(base + PV_T_OFF + (src & 15));
 #pragma unroll
-                    for (int h = 0; h < NREP; h++) {
-                        m[h] = stp[2 * h];
-                        sum[h] = stp[2 * h + 1];
+                    for (int n = 0; n < NP; n++) {
+                        if (len[n] == 0) continue;
+                        const int i = n / NREP, h = n % NREP;
+                        const uintptr_t src = reinterpret_cast<uintptr_t>(
+                            a.stats + ((size_t)(r0 + i) * a.n_heads + (size_t)it.kvh * NREP) * 2);
+                        const float *stp = reinterpret_cast<const float *>(base + PV_T_OFF + i * stat_slot + (src & 15));
+                        m[n] = stp[2 * h];
+                        sum[n] = stp[2 * h + 1];
                     }
                 }
                 const int rows = min(PV_TILE, t1 - tt);
@@ -967,10 +1031,10 @@ __global__ void __launch_bounds__(PV_THREADS, 1)
                 unsigned char *prow = base + PV_P_OFF + (t / 64) * 2048 + (t % 8) * 2;
                 const int c16 = (t % 64) / 8;
 #pragma unroll
-                for (int h = 0; h < NREP; h++) {
-                    if (h % PV_GROUPS != grp) continue;
-                    const float p = t < rows ? round_bf16(expf(s_st[h * PV_TILE + t] - m[h]) / sum[h]) : 0.0f;
-                    *reinterpret_cast<bf16 *>(prow + h * 128 + ((c16 ^ (h & 7)) << 4)) = __float2bfloat16(p);
+                for (int n = 0; n < NP; n++) {
+                    if (n % PV_GROUPS != grp) continue;
+                    const float p = tt + t < len[n] ? round_bf16(expf(s_st[n * PV_TILE + t] - m[n]) / sum[n]) : 0.0f;
+                    *reinterpret_cast<bf16 *>(prow + n * 128 + ((c16 ^ (n & 7)) << 4)) = __float2bfloat16(p);
                 }
                 if (t >= rows) {  // V rows past the sequence: zero both halves of row t, split over the groups
                     for (int half = grp; half < 2; half += PV_GROUPS) {
@@ -1198,15 +1262,24 @@ int launch_pv_tc(const AttnArgs &a, cudaStream_t s) {
     // kind::f16: fp32 accumulate, bf16 A (MN-major) and B (K-major), N = 16, M = 128
     pl.idesc = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 15) | ((uint32_t)(16 >> 3) << 17) |
                ((uint32_t)(128 >> 4) << 24);
+    // rows that share one cache (sequence stride 0: a prompt's rows at consecutive positions) go
+    // 16 / NREP to an item, so that one V tile in shared memory serves all of them
+    pl.rows = a.kv.seq == 0 && a.B > 1 ? 16 / NREP : 1;
     CUtensorMap mv;
     if (!make_map_strided(&mv, a.vc, cache_map_rows(a), a.kv.pos, a.kv.pos, PV_TILE)) return Q3_ERR_ARG;
     const size_t base = 1024 + (size_t)PV_STAGES * PV_STAGE_BYTES + 256 + (size_t)ITEM_TAB_OFF(a.B) * 4;
     pl.tab_cap = base < SMEM_CTA_MAX ? (int)std::min<size_t>(ITEM_TAB_MAX, (SMEM_CTA_MAX - base) / 8) : 0;
     const size_t smem = base + (size_t)pl.tab_cap * 8;
-    Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP>), smem));
-    const long long max_items = (long long)a.B * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
+    const long long max_items =
+        (long long)((a.B + pl.rows - 1) / pl.rows) * a.n_kv * ((a.max_seq + a.chunk_b - 1) / a.chunk_b);
     const int grid = (int)std::min<long long>(max_items, num_sms());
-    Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP>, dim3(grid), dim3(PV_THREADS), smem, s, 1, mv, a, pl));
+    if (pl.rows == 1) {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP, 1>), smem));
+        Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP, 1>, dim3(grid), dim3(PV_THREADS), smem, s, 1, mv, a, pl));
+    } else {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_pv_tc_kernel<NREP, 16 / NREP>), smem));
+        Q3_TRY_LAUNCH(launch(attn_pv_tc_kernel<NREP, 16 / NREP>, dim3(grid), dim3(PV_THREADS), smem, s, 1, mv, a, pl));
+    }
     return Q3_OK;
 }
 

@@ -199,3 +199,37 @@ def test_batched_embedding_and_token_range():
     _lib.call("q3_embedding_batched", out.data_ptr(), table.data_ptr(), bad.data_ptr(), 2, H, V, stream())
     assert torch.equal(out[0], table[3]) and not out[1].view(torch.int16).any()
     assert q3.device_error() == 2  # token-range flag, and no read outside the table
+
+
+# Rows of one prompt share one cache (sequence stride 0) at consecutive positions: the split
+# attention then gives an item 16 / NREP rows, so that one V tile in shared memory serves all of
+# them (their query heads side by side as the MMA's 16 columns). Each row must come out exactly as
+# when it has a cache of its own: the same probabilities, the same chunks, and the tensor cores
+# sum each column on its own. Row counts that leave a partial last group, and rows whose ends fall
+# in different 512-position chunks.
+@pytest.mark.parametrize("rows,n_heads,n_kv,p0", [(7, 32, 8, 3000), (64, 32, 8, 500), (5, 16, 8, 1021),
+                                                   (9, 64, 8, 130)])
+def test_prompt_rows_sharing_one_cache_match_separate_caches(rows, n_heads, n_kv, p0):
+    hd, max_seq = 128, 4096
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + n_heads + p0)
+    kvd = n_kv * hd
+    kc1 = rn(g, max_seq, kvd)  # [pos][kv heads * hd]: the reference layout, one cache
+    vc1 = rn(g, max_seq, kvd)
+    q = rn(g, rows, n_heads * hd)
+    positions = [p0 + i for i in range(rows)]
+    pos = torch.tensor(positions, dtype=torch.int32, device="cuda")
+    scale = float(np.float32(1.0 / math.sqrt(hd)))
+    nbytes = _lib.load().q3_attention_scratch_bytes(rows, n_heads, n_kv, hd, max_seq)
+    shared = torch.empty(rows, n_heads * hd, dtype=torch.bfloat16, device="cuda")
+    scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    _lib.call("q3_attention_batched", shared.data_ptr(), q.data_ptr(), kc1.data_ptr(), vc1.data_ptr(), 0, kvd, hd,
+              scratch.data_ptr(), pos.data_ptr(), rows, n_heads, n_kv, hd, max_seq, scale, stream())
+    kc = kc1.unsqueeze(0).repeat(rows, 1, 1).contiguous()  # every row its own copy
+    vc = vc1.unsqueeze(0).repeat(rows, 1, 1).contiguous()
+    own = torch.empty_like(shared)
+    scratch.zero_()
+    _lib.call("q3_attention_batched", own.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), max_seq * kvd, kvd,
+              hd, scratch.data_ptr(), pos.data_ptr(), rows, n_heads, n_kv, hd, max_seq, scale, stream())
+    torch.cuda.synchronize()
+    assert torch.equal(shared, own), f"{int((shared != own).sum())} of {shared.numel()} elements differ"
+    assert q3.device_error() == 0
