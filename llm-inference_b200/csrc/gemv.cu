@@ -15,7 +15,7 @@
 // and are marked evict-first in L2, then runs the reference's FMA chain over them. The first
 // batch of a warp's first row is loaded before the programmatic-dependency wait, because weights
 // never depend on the previous kernel, and the next row's first batch is loaded before the
-// current row's reduction and store. x is read through L1, where every warp of the SM finds it.
+// current row's reduction and store.
 //
 // The input vector x is the previous launch's output. After the programmatic-dependency wait every
 // CTA copies it into shared memory with cp.async, all of its 16-byte pieces in flight at once (one
