@@ -569,9 +569,11 @@ __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant_
 // flight, which is what keeps HBM busy -- and then computes, for each of its two rows and every
 // query head of the kv group, the reference's dot product: one fp32 chain per (row, head), dims
 // in order, one fused multiply-add each (src/kernels.cu:455-460, where nvcc fuses
-// `dot += q * k`), then s = round_bf16(round_bf16(dot) * scale). The group's query heads sit in
-// shared memory as fp32 [dim][head], so one vector load gives a dim's value for every head and
-// serves both rows. The swizzle puts the 16-byte chunk c of row r at chunk c ^ (r % 8): a warp's
+// `dot += q * k`), then s = round_bf16(round_bf16(dot) * scale). Each step is one
+// mixed-precision fma of the bf16 q and k into the fp32 chain (fma_bb): no conversions, and bit
+// for bit the fp32 fma of the converted operands. The group's query heads sit in shared memory as
+// bf16 [dim][head], so one vector load gives two dims' values for every head and serves both
+// rows. The swizzle puts the 16-byte chunk c of row r at chunk c ^ (r % 8): a warp's
 // 32 threads reading the same logical chunk of 32 consecutive rows need only the four wavefronts
 // of their 512 bytes.
 constexpr int SX_TILE = 128;
@@ -616,31 +618,60 @@ __device__ __forceinline__ bool group_any(int group, bool v) {
     return r != 0;
 }
 
-// q values of one dim for the NREP heads: one shared-memory vector load
+// q words of two consecutive dims d, d + 1 for the NREP heads, bf16 [dim][head]: with NREP >= 2
+// word i of dim d holds heads 2i, 2i + 1 and dim d + 1's words follow; with one head the word
+// holds dim d in its low half and d + 1 in its high half. One shared-memory vector load.
 template <int NREP>
-struct QVec {
-    float v[NREP];
+struct QPair {
+    uint32_t w[NREP == 1 ? 1 : NREP];
 };
 template <int NREP>
-__device__ __forceinline__ QVec<NREP> load_q(const float *p) {
-    QVec<NREP> q;
-    if constexpr (NREP % 4 == 0) {
-#pragma unroll
-        for (int i = 0; i < NREP; i += 4) {
-            const float4 f = *reinterpret_cast<const float4 *>(p + i);
-            q.v[i] = f.x;
-            q.v[i + 1] = f.y;
-            q.v[i + 2] = f.z;
-            q.v[i + 3] = f.w;
-        }
+__device__ __forceinline__ QPair<NREP> load_q2(const bf16 *p) {
+    QPair<NREP> q;
+    if constexpr (NREP == 8) {
+        const uint4 u0 = *reinterpret_cast<const uint4 *>(p), u1 = *reinterpret_cast<const uint4 *>(p + 8);
+        q.w[0] = u0.x, q.w[1] = u0.y, q.w[2] = u0.z, q.w[3] = u0.w;
+        q.w[4] = u1.x, q.w[5] = u1.y, q.w[6] = u1.z, q.w[7] = u1.w;
+    } else if constexpr (NREP == 4) {
+        const uint4 u = *reinterpret_cast<const uint4 *>(p);
+        q.w[0] = u.x, q.w[1] = u.y, q.w[2] = u.z, q.w[3] = u.w;
     } else if constexpr (NREP == 2) {
-        const float2 f = *reinterpret_cast<const float2 *>(p);
-        q.v[0] = f.x;
-        q.v[1] = f.y;
+        const uint2 u = *reinterpret_cast<const uint2 *>(p);
+        q.w[0] = u.x, q.w[1] = u.y;
     } else {
-        q.v[0] = p[0];
+        q.w[0] = *reinterpret_cast<const uint32_t *>(p);
     }
     return q;
+}
+
+// acc = fma(q, k, acc) with q and k the low or high bf16 halves of q2 and k2. sm_100's
+// mixed-precision fma takes the bf16 operands as they are: their product is exact in fp32 (8 + 8
+// significant bits) and the one rounding of q * k + acc is that of fmaf(float(q), float(k), acc),
+// so the chain is the reference's bit for bit with no operand converted first.
+__device__ __forceinline__ void fma_bb(float &acc, uint32_t q2, bool qhi, uint32_t k2, bool khi) {
+#define Q3_FMA_BB(QR, KR)                                                                  \
+    asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %1;\n\tmov.b32 {kl, kh}, %2;\n\t" \
+        "fma.rn.f32.bf16 %0, " QR ", " KR ", %0;\n\t}"                                       \
+        : "+f"(acc)                                                                        \
+        : "r"(q2), "r"(k2))
+    if (qhi) {
+        if (khi) Q3_FMA_BB("qh", "kh");
+        else Q3_FMA_BB("qh", "kl");
+    } else {
+        if (khi) Q3_FMA_BB("ql", "kh");
+        else Q3_FMA_BB("ql", "kl");
+    }
+#undef Q3_FMA_BB
+}
+
+// Dim d (0 or 1) of the pair for every head of one row; k is the row's word holding both dims.
+template <int NREP>
+__device__ __forceinline__ void fma_heads_bb(float (&acc)[NREP], const QPair<NREP> &q, int d, uint32_t kw) {
+#pragma unroll
+    for (int h = 0; h < NREP; h++) {
+        if constexpr (NREP == 1) fma_bb(acc[h], q.w[0], d == 1, kw, d == 1);
+        else fma_bb(acc[h], q.w[d * (NREP / 2) + h / 2], (h & 1) == 1, kw, d == 1);
+    }
 }
 
 template <int NREP, int G>
@@ -700,16 +731,16 @@ __global__ void __launch_bounds__(sx_threads(G), 1)
     // ---------------- consumers: group g takes items g, g + G, ...
     const int group = (warp - 1) / SX_GWARPS;
     const int gt = threadIdx.x - 32 - group * SX_GWARPS * 32;  // 0..63
-    float *q_s = q_all + group * NREP * hd;                    // [hd][NREP]
+    bf16 *q_s = reinterpret_cast<bf16 *>(q_all + group * NREP * hd);  // [hd][NREP] (half the region)
     int qb = -1, qk = -1;
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
     for (int k = group; k < n && !failed; k += G) {
         const Item it = item_k(a, prefix, SX_TILE, tab, tabbed, i0, k, cur);
-        if (it.b != qb || it.kvh != qk) {  // the group's query heads, as fp32, dims outermost
+        if (it.b != qb || it.kvh != qk) {  // the group's query heads, bf16, dims outermost
             group_sync(group);             // nobody still reads the previous ones
             const bf16 *qg = a.q + (size_t)it.b * a.q_stride + (size_t)it.kvh * NREP * hd;
-            for (int j = gt; j < NREP * hd; j += SX_GWARPS * 32) q_s[(j % hd) * NREP + j / hd] = __bfloat162float(qg[j]);
+            for (int j = gt; j < NREP * hd; j += SX_GWARPS * 32) q_s[(j % hd) * NREP + j / hd] = qg[j];
             group_sync(group);
             qb = it.b;
             qk = it.kvh;
@@ -740,19 +771,19 @@ __global__ void __launch_bounds__(sx_threads(G), 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);  // the rows are in registers: the box is free
             if (failed) break;
-            const float *qd = q_s + half * 64 * NREP;
+            const bf16 *qd = q_s + half * 64 * NREP;
 #pragma unroll
             for (int c = 0; c < 8; c++) {
+                const uint4 wa = *reinterpret_cast<const uint4 *>(&ka[c]);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(&kb[c]);
+                const uint32_t pa[4] = {wa.x, wa.y, wa.z, wa.w}, pb[4] = {wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    const QVec<NREP> q = load_q<NREP>(qd + (c * 8 + e) * NREP);
-                    const float fa = e & 1 ? __high2float(ka[c].h[e / 2]) : __low2float(ka[c].h[e / 2]);
-                    const float fb = e & 1 ? __high2float(kb[c].h[e / 2]) : __low2float(kb[c].h[e / 2]);
-#pragma unroll
-                    for (int h = 0; h < NREP; h++) {
-                        acc_a[h] = __fmaf_rn(q.v[h], fa, acc_a[h]);
-                        acc_b[h] = __fmaf_rn(q.v[h], fb, acc_b[h]);
-                    }
+                for (int e = 0; e < 8; e += 2) {
+                    const QPair<NREP> q = load_q2<NREP>(qd + (c * 8 + e) * NREP);
+                    fma_heads_bb<NREP>(acc_a, q, 0, pa[e / 2]);
+                    fma_heads_bb<NREP>(acc_b, q, 0, pb[e / 2]);
+                    fma_heads_bb<NREP>(acc_a, q, 1, pa[e / 2]);
+                    fma_heads_bb<NREP>(acc_b, q, 1, pb[e / 2]);
                 }
             }
         }
