@@ -277,7 +277,12 @@ typedef struct q3_engine_buffers {
     int *history;          /* [history_cap][batch] tokens of steps 0, 1, ... */
     int *step;             /* steps run since creation */
     int batch, max_seq, history_cap;
-    int launches_per_step; /* kernel launches in the captured step (0 before q3_engine_capture) */
+    int launches_per_step; /* kernel launches in the captured step the next q3_engine_step runs
+                              (0 before q3_engine_capture) */
+    int split_from;        /* with the fused RoPE + attention launch (small batches): the position
+                              of the longest sequence from which a step runs the split-KV kernels
+                              instead, captured as a second graph; -1 when one path serves every
+                              position */
 } q3_engine_buffers;
 
 enum {

@@ -435,6 +435,58 @@ __global__ void __launch_bounds__(128 * NREP) attn_stats_kernel(const __grid_con
     }
 }
 
+// Few (sequence, kv head) groups (batch 1 and 2 at 8 kv heads): the same statistics with one
+// 128-thread CTA per (sequence, query head), so that B * n_heads SMs share the reads. The CTA
+// first copies the head's scores into shared memory (every 16-byte piece in flight at once: one
+// round trip to L2), then thread s runs slot s's chain from there, its loads and expf calls
+// independent of the chain's additions and so issued ahead of them. Same values in the same
+// order as attn_stats_kernel: the max is order-free, and each slot still adds its positions s,
+// s + 128, ... serially before the xor tree and the four warp totals in order.
+__global__ void __launch_bounds__(128) attn_stats_row_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) float row[];  // this head's len scores
+    __shared__ float red[4];
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.x / a.n_heads, hq = blockIdx.x % a.n_heads;
+    const int len = seq_len(a, b);
+    if (len == 0) return;
+    const int slot = threadIdx.x, lane = slot % 32, w = slot / 32;
+    const float *sc = a.scores + ((size_t)b * a.n_heads + hq) * a.ld;
+    if ((reinterpret_cast<uintptr_t>(sc) & 15) == 0) {
+        const int n4 = len / 4;
+        for (int i = slot; i < n4; i += 128) cp_async16(row + 4 * i, sc + 4 * i);
+        for (int i = 4 * n4 + slot; i < len; i += 128) cp_async4(row + i, sc + i);
+    } else {
+        for (int i = slot; i < len; i += 128) cp_async4(row + i, sc + i);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    float mx = -INFINITY;
+#pragma unroll 8
+    for (int t = slot; t < len; t += 128) mx = fmaxf(mx, row[t]);
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) red[w] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();  // red is reused for the sums
+    float sm = 0.0f;
+#pragma unroll 8
+    for (int t = slot; t < len; t += 128) sm += expf(row[t] - mx);
+    for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+    if (lane == 0) red[w] = sm;
+    __syncthreads();
+    if (slot == 0) {
+        float r = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4; i++) r += red[i];
+        float *st = a.stats + ((size_t)b * a.n_heads + hq) * 2;
+        st[0] = mx;
+        st[1] = r;
+    }
+}
+constexpr size_t STATS_ROW_SMEM_MAX = 200 * 1024;
+
 // ------------------------------------------------------------------ pv
 template <int NREP, int DPT>
 __global__ void __launch_bounds__(THREADS) attn_pv_kernel(const __grid_constant__ AttnArgs a) {
@@ -681,7 +733,7 @@ __global__ void __launch_bounds__(sx_threads(G), 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     unsigned char *smem = align_shared<1024>(smem_raw);
     const int hd = a.head_dim;
-    float *q_all = reinterpret_cast<float *>(smem + (size_t)SX_STAGES * SX_BOX);  // [G][hd][NREP]
+    bf16 *q_all = reinterpret_cast<bf16 *>(smem + (size_t)SX_STAGES * SX_BOX);  // [G][hd][NREP]
     uint64_t *full = reinterpret_cast<uint64_t *>(q_all + G * NREP * hd);
     uint64_t *empty = full + SX_STAGES;
     int *prefix = reinterpret_cast<int *>(empty + SX_STAGES);
@@ -731,7 +783,7 @@ __global__ void __launch_bounds__(sx_threads(G), 1)
     // ---------------- consumers: group g takes items g, g + G, ...
     const int group = (warp - 1) / SX_GWARPS;
     const int gt = threadIdx.x - 32 - group * SX_GWARPS * 32;  // 0..63
-    bf16 *q_s = reinterpret_cast<bf16 *>(q_all + group * NREP * hd);  // [hd][NREP] (half the region)
+    bf16 *q_s = q_all + group * NREP * hd;                      // [hd][NREP]
     int qb = -1, qk = -1;
     const int sw = gt & 7;  // rows gt and gt + 64 share the swizzle phase
     bool failed = false;
@@ -1264,7 +1316,7 @@ int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
     if (!make_map_strided(&mk, a.kc, cache_map_rows(a), a.kv.pos, a.kv.pos, SX_TILE)) return Q3_ERR_ARG;
     const int G = sx_groups(pl.halves);
     if (pl.halves < 1 || pl.halves > 4 || SX_STAGES % (G * pl.halves) != 0) return Q3_ERR_SHAPE;
-    const size_t base = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)G * NREP * a.head_dim * 4 +
+    const size_t base = 1024 + (size_t)SX_STAGES * SX_BOX + (size_t)G * NREP * a.head_dim * 2 +
                         2 * SX_STAGES * 8 + (size_t)ITEM_TAB_OFF(a.B) * 4;
     pl.tab_cap = base < SMEM_CTA_MAX ? (int)std::min<size_t>(ITEM_TAB_MAX, (SMEM_CTA_MAX - base) / 8) : 0;
     const size_t smem = base + (size_t)pl.tab_cap * 8;
@@ -1278,8 +1330,15 @@ int launch_scores_exact(const AttnArgs &a, cudaStream_t s) {
 }
 
 // One block of 128 * NREP threads per (sequence, kv head).
+// Fewer (sequence, kv head) groups than SMs: one CTA per (sequence, query head) instead.
 template <int NREP>
 int launch_stats(const AttnArgs &a, cudaStream_t s) {
+    const size_t row_smem = (size_t)a.max_seq * 4;
+    if (a.B * a.n_kv < num_sms() && row_smem <= STATS_ROW_SMEM_MAX) {
+        Q3_TRY_LAUNCH(allow_smem(reinterpret_cast<const void *>(attn_stats_row_kernel), row_smem));
+        Q3_TRY_LAUNCH(launch(attn_stats_row_kernel, dim3(a.B * a.n_heads), dim3(128), row_smem, s, 1, a));
+        return Q3_OK;
+    }
     Q3_TRY_LAUNCH(launch(attn_stats_kernel<NREP>, dim3(a.B * a.n_kv), dim3(128 * NREP), 0, s, 1, a));
     return Q3_OK;
 }

@@ -21,6 +21,7 @@
 #include <vector>
 
 #include <algorithm>
+#include <climits>
 
 #include "common.cuh"
 
@@ -81,6 +82,11 @@ struct q3_engine {
     AttnSplit split;
     // small batches: RoPE and attention in one launch (attn_fused.cu), this many chunks per head
     int fused_chunks = 0;
+    // ... up to this position of the longest sequence; from it on a step runs the split-KV
+    // kernels, captured as a second graph (INT_MAX: the fused launch throughout)
+    int split_from = INT_MAX;
+    long long pos_hint = 0;   // the largest position the next step attends up to (host's count)
+    bool split_now = false;   // enqueue the split-KV kernels even where the fused launch applies
     // decode-loop state
     int *next_token, *pos, *out_token, *history, *step;
     int *pf_token, *pf_pos;  // prefill: one chunk's token ids and positions
@@ -90,8 +96,10 @@ struct q3_engine {
     DsParams mkp = {};
     int mk_grid = 0;
     int *host_io;  // pinned: [2B] for token/position uploads, [B] for downloads
-    cudaGraphExec_t graph;
-    int graph_kernels;  // kernel nodes of the captured step
+    cudaGraphExec_t graph = nullptr;
+    int graph_kernels = 0;  // kernel nodes of the captured step
+    cudaGraphExec_t graph_split = nullptr;  // the step with split-KV attention, when split_from < max_seq
+    int graph_split_kernels = 0;
     cudaStream_t own_stream;  // created when the caller passes the legacy default stream
     std::vector<void *> allocations;
 };
@@ -104,6 +112,9 @@ int alloc(q3_engine *e, void **p, size_t bytes) {
     e->allocations.push_back(*p);
     return Q3_OK;
 }
+
+// positions per fused-attention CTA from which a step runs the split-KV kernels instead
+constexpr int FUSED_SPLIT_PER_CTA = 600;
 
 #define TRY(expr)                     \
     do {                              \
@@ -125,7 +136,7 @@ int enqueue_layers(q3_engine *e, int rows, const int *tok, const int *pos, int c
     cudaStream_t s = e->stream;
     const bool exact_attn = (e->flags & Q3_ENGINE_EXACT_ATTENTION) != 0;
     // rows of a prompt share one cache and read each other's new rows: not in one fused launch
-    const bool fused = e->fused_chunks > 0 && !shared_cache;
+    const bool fused = e->fused_chunks > 0 && !shared_cache && !e->split_now;
     // one row: the batch-1 projections that read a normed input normalize it themselves
     const bool norm_in_gemv = rows == 1 && H <= 8192;
     const float eps = c.rms_norm_eps;
@@ -185,8 +196,38 @@ int enqueue_step(q3_engine *e) {
     return Q3_OK;
 }
 
+// Captures one decode step (split: the split-KV attention kernels throughout) into *out.
+int capture_step(q3_engine *e, bool split, cudaGraphExec_t *out, int *kernels_out) {
+    cudaGraph_t g;
+    int r = record_cuda_error(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+    if (r != Q3_OK) return r;
+    e->split_now = split;
+    const int st = enqueue_step(e);
+    e->split_now = false;
+    r = record_cuda_error(cudaStreamEndCapture(e->stream, &g));
+    if (st != Q3_OK) {
+        if (r == Q3_OK) cudaGraphDestroy(g);
+        return st;
+    }
+    if (r != Q3_OK) return r;
+    size_t n_nodes = 0;
+    cudaGraphGetNodes(g, nullptr, &n_nodes);
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    int kernels = 0;
+    if (n_nodes && cudaGraphGetNodes(g, nodes.data(), &n_nodes) == cudaSuccess)
+        for (auto nd : nodes) {
+            cudaGraphNodeType t;
+            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+        }
+    *kernels_out = kernels;
+    r = record_cuda_error(cudaGraphInstantiate(out, g, 0));
+    cudaGraphDestroy(g);
+    return r;
+}
+
 void release(q3_engine *e) {
     if (e->graph) cudaGraphExecDestroy(e->graph);
+    if (e->graph_split) cudaGraphExecDestroy(e->graph_split);
     if (e->own_stream) cudaStreamDestroy(e->own_stream);
     for (void *p : e->allocations) cudaFree(p);
     if (e->host_io) cudaFreeHost(e->host_io);
@@ -273,11 +314,13 @@ int q3_engine_create(const q3_config *cfg, const q3_weights *w, int batch, int m
     A((void **)&e->pf_pos, B * 4);
     if (!mk && !(flags & (Q3_ENGINE_EXACT_ATTENTION | Q3_ENGINE_SPLIT_ATTENTION)))
         e->fused_chunks = fused_chunks(batch, c.n_heads, c.n_kv_heads, c.head_dim, max_seq);
-    // With a thousand positions or more per cluster CTA the split-KV kernels, which spread every
-    // row over all SMs, are the faster path (measured on B200: Qwen3-1.7B, 8 sequences at position
-    // 2048, two-CTA clusters: 3544 tok/s fused, 3698 split; with a few hundred positions per CTA the
-    // fused launch wins, e.g. Qwen3-4B batch 1 at position 2048: 413 against 357).
-    if (e->fused_chunks > 0 && max_seq / e->fused_chunks >= 1024) e->fused_chunks = 0;
+    // From about 600 positions per cluster CTA on, the split-KV kernels, which spread every row
+    // over all SMs, are the faster path; below it the single fused launch is. Measured on B200,
+    // tok/s fused against split: Qwen3-4B batch 1 (10-CTA clusters) at position 256 454 / 375,
+    // 4096 364 / 344, 6144 336 / 335, 8192 306 / 328; Qwen3-1.7B at position 2048, 8 sequences
+    // (2-CTA clusters, 1024 per CTA) 3544 / 3698, 4 sequences (4-CTA, 512 per CTA) 2088 / 2027.
+    // Both steps are captured and q3_engine_step picks one by the host's count of positions.
+    if (e->fused_chunks > 0) e->split_from = FUSED_SPLIT_PER_CTA * e->fused_chunks;
     if (mk) {
         e->mk = true;
         DsParams &p = e->mkp;
@@ -375,45 +418,31 @@ int q3_engine_capture(q3_engine *e) {
         e->graph_kernels = 1;
         return Q3_OK;
     }
-    if (e->graph) {
-        cudaGraphExecDestroy(e->graph);
-        e->graph = nullptr;
-    }
-    cudaGraph_t g;
-    int r = record_cuda_error(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
-    if (r != Q3_OK) return r;
-    const int st = enqueue_step(e);
-    r = record_cuda_error(cudaStreamEndCapture(e->stream, &g));
-    if (st != Q3_OK) {
-        if (r == Q3_OK) cudaGraphDestroy(g);
-        return st;
-    }
-    if (r != Q3_OK) return r;
-    size_t n_nodes = 0;
-    cudaGraphGetNodes(g, nullptr, &n_nodes);
-    std::vector<cudaGraphNode_t> nodes(n_nodes);
-    int kernels = 0;
-    if (n_nodes && cudaGraphGetNodes(g, nodes.data(), &n_nodes) == cudaSuccess)
-        for (auto nd : nodes) {
-            cudaGraphNodeType t;
-            if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) kernels++;
+    for (cudaGraphExec_t *g : {&e->graph, &e->graph_split})
+        if (*g) {
+            cudaGraphExecDestroy(*g);
+            *g = nullptr;
         }
-    e->graph_kernels = kernels;
-    r = record_cuda_error(cudaGraphInstantiate(&e->graph, g, 0));
-    cudaGraphDestroy(g);
-    return r;
+    TRY(capture_step(e, false, &e->graph, &e->graph_kernels));
+    if (e->split_from < e->max_seq) TRY(capture_step(e, true, &e->graph_split, &e->graph_split_kernels));
+    return Q3_OK;
 }
 
 int q3_engine_step(q3_engine *e, int n_steps) {
     if (!e || n_steps < 0) return Q3_ERR_ARG;
     for (int i = 0; i < n_steps; i++) {
-        if (e->graph) {
-            int r = record_cuda_error(cudaGraphLaunch(e->graph, e->stream));
+        const bool split = e->pos_hint >= e->split_from;
+        cudaGraphExec_t g = split && e->graph_split ? e->graph_split : e->graph;
+        if (g) {
+            int r = record_cuda_error(cudaGraphLaunch(g, e->stream));
             if (r != Q3_OK) return r;
         } else {
-            int r = enqueue_step(e);
+            e->split_now = split;
+            const int r = enqueue_step(e);
+            e->split_now = false;
             if (r != Q3_OK) return r;
         }
+        e->pos_hint++;  // every row's position advances by one (argmax_rows)
     }
     return Q3_OK;
 }
@@ -429,6 +458,7 @@ int q3_engine_set_state(q3_engine *e, const int *tokens, const int *positions) {
     if (r != Q3_OK) return r;
     memcpy(io, tokens, e->B * sizeof(int));
     memcpy(io + e->B, positions, e->B * sizeof(int));
+    e->pos_hint = *std::max_element(positions, positions + e->B);
     r = record_cuda_error(cudaMemcpyAsync(e->next_token, io, e->B * sizeof(int), cudaMemcpyHostToDevice, e->stream));
     if (r == Q3_OK)
         r = record_cuda_error(cudaMemcpyAsync(e->pos, io + e->B, e->B * sizeof(int), cudaMemcpyHostToDevice, e->stream));
@@ -470,6 +500,7 @@ int q3_engine_prefill(q3_engine *e, int seq, const int *tokens, int n_tokens, in
     int r = record_cuda_error(cudaStreamSynchronize(e->stream));
     if (r != Q3_OK) return r;
     io[2 * e->B] = start_pos + n_tokens;
+    e->pos_hint = std::max(e->pos_hint, (long long)start_pos + n_tokens);
     r = record_cuda_error(cudaMemcpyAsync(e->pos + seq, io + 2 * e->B, sizeof(int), cudaMemcpyHostToDevice, e->stream));
     if (r == Q3_OK) r = record_cuda_error(cudaStreamSynchronize(e->stream));
     return r;
@@ -512,7 +543,9 @@ int q3_engine_info(const q3_engine *e, q3_engine_buffers *out) {
     out->batch = e->B;
     out->max_seq = e->max_seq;
     out->history_cap = e->history_cap;
-    out->launches_per_step = e->graph_kernels;
+    const bool split = e->pos_hint >= e->split_from && e->graph_split;
+    out->launches_per_step = split ? e->graph_split_kernels : e->graph_kernels;
+    out->split_from = e->split_from < e->max_seq ? e->split_from : -1;
     return Q3_OK;
 }
 

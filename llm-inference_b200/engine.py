@@ -36,7 +36,7 @@ class Q3Weights(ctypes.Structure):
 class Q3EngineBuffers(ctypes.Structure):
     _fields_ = [("x", _B), ("logits", _B), ("key_cache", _B), ("value_cache", _B), ("next_token", _B), ("pos", _B),
                 ("out_token", _B), ("history", _B), ("step", _B), ("batch", ctypes.c_int), ("max_seq", ctypes.c_int),
-                ("history_cap", ctypes.c_int), ("launches_per_step", ctypes.c_int)]
+                ("history_cap", ctypes.c_int), ("launches_per_step", ctypes.c_int), ("split_from", ctypes.c_int)]
 
 
 def q3_config(s: ckpt.Qwen3Shape) -> Q3Config:
@@ -273,7 +273,14 @@ class Engine:
         call("q3_engine_info", self.handle, ctypes.byref(self.info))
 
     def launches_per_step(self) -> int:
+        """Kernel launches of the captured step that the next step() runs."""
+        call("q3_engine_info", self.handle, ctypes.byref(self.info))
         return self.info.launches_per_step
+
+    def split_from(self) -> int:
+        """Position from which a step runs the split-KV attention instead of the fused launch
+        (-1: one path for every position)."""
+        return self.info.split_from
 
     def step(self, n: int = 1):
         call("q3_engine_step", self.handle, n)

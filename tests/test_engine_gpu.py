@@ -124,3 +124,43 @@ def test_device_loop_matches_protocol(model):
     assert loop.positions().cpu().tolist() == [N_PROMPT + N_NEW - 1] * batch
     loop.close()
     assert q3.device_error() == 0
+
+
+def test_engine_switches_to_split_attention_at_long_context():
+    """A batch-1 engine runs the fused RoPE + attention launch up to split_from and the split-KV
+    kernels from there on, as a second captured graph. Qwen3-4B shapes cut to 2 layers, caches
+    filled identically: from split_from on its logits equal those of an engine created with
+    split attention throughout, bit for bit (same kernels); below it they agree to the fused
+    P.V's reordering; the device loop crosses the switch with positions advancing one a step."""
+    full = checkpoint.PRESETS["qwen3-4b"]
+    shape = checkpoint.Qwen3Shape(full.hidden_size, full.intermediate_size, 2, full.num_attention_heads,
+                                  full.num_key_value_heads, full.head_dim, full.vocab_size)
+    max_seq = 8192
+    w = DeviceWeights.random(shape, seed=3)
+    auto = Engine(w, batch=1, max_seq=max_seq, history_cap=16)
+    split = Engine(w, batch=1, max_seq=max_seq, history_cap=16, split_attention=True)
+    sf = auto.split_from()
+    assert 0 < sf < max_seq, sf
+    assert split.split_from() == -1
+    for e in (auto, split):
+        e.fill_kv_normal(max_seq, seed=29)
+        e.capture()
+    auto.forward([321], [sf + 3])
+    split.forward([321], [sf + 3])
+    torch.cuda.synchronize()
+    assert torch.equal(auto.logits().view(torch.int16), split.logits().view(torch.int16))
+    assert auto.launches_per_step() == split.launches_per_step()
+    auto.forward([321], [sf - 5])
+    split.forward([321], [sf - 5])
+    torch.cuda.synchronize()
+    assert auto.launches_per_step() < split.launches_per_step()  # the fused launch again
+    a, s = auto.logits().float(), split.logits().float()
+    rel = float(((a - s).pow(2).mean() / s.pow(2).mean()).sqrt())
+    assert rel < 1e-2, rel
+    auto.set_state([7], [sf - 2])
+    auto.step(4)
+    torch.cuda.synchronize()
+    assert auto.positions().cpu().tolist() == [sf + 2]
+    for e in (auto, split):
+        e.close()
+    assert q3.device_error() == 0

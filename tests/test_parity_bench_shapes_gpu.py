@@ -310,3 +310,49 @@ def test_split_scores_bit_identical_to_serial_dot(case):
            sum(p + 1 for p in positions) * n_heads, "bit-identical")
     assert mismatches == 0, f"{mismatches} scores differ from the serial dot"
     assert q3.device_error() == 0
+
+
+def test_split_stats_and_outputs_do_not_depend_on_batch():
+    """Softmax statistics of the split path, bit for bit, whichever kernel computes them: with 20
+    sequences (160 (sequence, kv head) groups, at least one per SM) attn_stats_kernel runs, one
+    CTA per group; with 1 or 2 sequences attn_stats_row_kernel runs, one CTA per query head.
+    Both must give the reference's max and slot-order sum (src/kernels.cu:406-436, 467-470), so
+    the same sequences' stats, scores and outputs must be identical in the three runs.
+    Positions include config 3's far end (8191) and a short row."""
+    n_heads, n_kv, hd, max_seq = 32, 8, 128, 8192
+    g = torch.Generator(device="cuda").manual_seed(77)
+    positions = [8191, 77] + [int(p) for p in torch.randint(0, max_seq, (18,), generator=g, device="cuda").tolist()]
+    big = len(positions)
+    kc = rn(g, big, max_seq, n_kv * hd)
+    vc = rn(g, big, max_seq, n_kv * hd)
+    q = rn(g, big, n_heads * hd)
+    kh, vh = head_major(kc, n_kv, hd), head_major(vc, n_kv, hd)
+    del kc, vc
+    scale = float(np.float32(1.0 / math.sqrt(hd)))
+    ld = (max_seq + 3) // 4 * 4
+
+    def run(batch):
+        pos = torch.tensor(positions[:batch], dtype=torch.int32, device="cuda")
+        nbytes = _lib.load().q3_attention_scratch_bytes(batch, n_heads, n_kv, hd, max_seq)
+        scratch = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+        out = torch.empty_like(q[:batch])
+        _lib.call("q3_attention_batched", out.data_ptr(), q.data_ptr(), kh.data_ptr(), vh.data_ptr(),
+                  n_kv * max_seq * hd, hd, max_seq * hd, scratch.data_ptr(), pos.data_ptr(), batch, n_heads, n_kv,
+                  hd, max_seq, scale, stream())
+        torch.cuda.synchronize()
+        o_stats = (batch * n_heads * ld * 4 + 255) // 256 * 256
+        sc = scratch[:batch * n_heads * ld * 4].view(torch.float32).view(batch, n_heads, ld)
+        st = scratch[o_stats:o_stats + batch * n_heads * 8].view(torch.float32).view(batch, n_heads, 2)
+        return sc.clone(), st.clone(), out
+
+    sc_big, st_big, out_big = run(big)
+    for batch in (1, 2):
+        sc, st, out = run(batch)
+        for b in range(batch):
+            n = positions[b] + 1
+            assert torch.equal(sc[b, :, :n].view(torch.int32), sc_big[b, :, :n].view(torch.int32)), f"scores, row {b}"
+        d = (st.view(torch.int32) != st_big[:batch].view(torch.int32)).sum().item()
+        record(f"split-path softmax stats, batch {batch} vs batch {big}", np.array([d]), st.numel(), "bit-identical")
+        assert d == 0, f"{d} of {st.numel()} stats differ"
+        assert torch.equal(out.view(torch.int16), out_big[:batch].view(torch.int16))
+    assert q3.device_error() == 0
