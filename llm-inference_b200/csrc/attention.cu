@@ -636,9 +636,11 @@ constexpr int SX_GWARPS = 2;  // warps per group: 64 threads, two rows each
 // its own items only, with the parity of the lap it expects; that is sound only if the stage's
 // previous box also belonged to this group (a box of another group may not have landed yet, and a
 // wait two phases ahead of the barrier passes at once). With items dealt round-robin that holds
-// when SX_STAGES is a multiple of groups x boxes per item: 6 groups for one or two boxes an item,
+// when SX_STAGES is a multiple of groups x boxes per item: 6 groups for one box an item (head_dim
+// 64), 3 for two (head_dim 128: each group then has two items in flight while it computes; with
+// six groups it had one, and the Qwen3-4B B = 32 decode step took 6.41 ms instead of 6.32),
 // 4 for three (head_dim 192), 3 for four (head_dim 256).
-constexpr int sx_groups(int halves) { return halves == 4 ? 3 : halves == 3 ? 4 : 6; }
+constexpr int sx_groups(int halves) { return halves == 1 ? 6 : halves == 3 ? 4 : 3; }
 static_assert(SX_STAGES % (sx_groups(1) * 1) == 0 && SX_STAGES % (sx_groups(2) * 2) == 0 &&
                   SX_STAGES % (sx_groups(3) * 3) == 0 && SX_STAGES % (sx_groups(4) * 4) == 0,
               "a ring stage must come back to the group that used it last");
