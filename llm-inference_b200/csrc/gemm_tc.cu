@@ -171,6 +171,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int S = a.stages;
 
+    // split-K: the S CTAs of a cluster share tile blockIdx.x / S, rank r takes K steps [k0, k1)
+    const int S_split = a.splits;
+    const int rank = S_split > 1 ? (int)cg::this_cluster().block_rank() : 0;
+    const int tile_base = S_split > 1 ? (int)blockIdx.x / S_split : (int)blockIdx.x;
+    const int tile_stride = S_split > 1 ? (int)gridDim.x / S_split : (int)gridDim.x;
+    const int k0 = a.nk * rank / S_split, k1 = a.nk * (rank + 1) / S_split;
+    const int nks = k1 - k0;
+    const int my_tiles = a.n_tiles > tile_base ? (a.n_tiles - 1 - tile_base) / tile_stride + 1 : 0;
+    const int total_steps = my_tiles * nks;
+    const uint32_t a_bytes = (uint32_t)a.R * BK * 2;
+    const uint32_t x_bytes = (uint32_t)a.Bp * BK * 2;
+    const CUtensorMap *maps[3] = {&tmA0, &tmA1, &tmA2};
+    const uint64_t stream_pol = policy_evict_first();  // weights are read once per step
+    // stage layout: [A sub-tiles 0..ksub-1][A1 sub-tiles (gate_up)][X sub-tiles 0..ksub-1]
+    auto stage_a = [&](int s, int i, int j) {
+        return smem + (size_t)s * a.stage_bytes + (size_t)(i * a.ksub + j) * a.a_tile_bytes;
+    };
+    auto stage_x = [&](int s, int j) {
+        return smem + (size_t)s * a.stage_bytes + (size_t)NA * a.ksub * a.a_tile_bytes + (size_t)j * x_bytes;
+    };
+    auto subs_of = [&](int ks) { return min(a.ksub, (a.K - ks * a.ksub * BK + BK - 1) / BK); };
+    auto issue_weights = [&](int it) {
+        const int s = it % S;
+        const int t = tile_base + (it / nks) * tile_stride;
+        const int ks = k0 + it % nks;
+        const int nsub = subs_of(ks);
+        int mat, row0;
+        tile_coords(a, t, mat, row0);
+        mbar_arrive_expect_tx(&full[s], nsub * (NA * a_bytes + x_bytes));
+        for (int j = 0; j < nsub; j++) {
+            const int col = (ks * a.ksub + j) * BK;
+            if (EPI == GATE_UP) {
+                tma_load_2d_stream(stage_a(s, 0, j), &tmA0, col, row0, &full[s], stream_pol);
+                tma_load_2d_stream(stage_a(s, 1, j), &tmA1, col, row0, &full[s], stream_pol);
+            } else {
+                tma_load_2d_stream(stage_a(s, 0, j), maps[mat], col, row0, &full[s], stream_pol);
+            }
+        }
+    };
+    const int pre = min(S, total_steps);
+
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; s++) {
             mbar_init(&full[s], 1);
@@ -186,6 +227,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (EPI == GATE_UP || EPI == QKV) prefetch_tmap(&tmA1);
         if (EPI == QKV) prefetch_tmap(&tmA2);
         if (EPI == RESIDUAL && a.res_tma) prefetch_tmap(&tmR);
+        // the first stages' weights: they depend on no earlier kernel, and nothing below (TMEM
+        // allocation, the block barrier, the dependency wait) has to come before them
+        for (int it = 0; it < pre; it++) issue_weights(it);
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -202,56 +246,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (a.splits > 1) cluster_arrive_relaxed();
     pdl_trigger();
 
-    // split-K: the S CTAs of a cluster share tile blockIdx.x / S, rank r takes K steps [k0, k1)
-    const int S_split = a.splits;
-    const int rank = S_split > 1 ? (int)cg::this_cluster().block_rank() : 0;
-    const int tile_base = S_split > 1 ? (int)blockIdx.x / S_split : (int)blockIdx.x;
-    const int tile_stride = S_split > 1 ? (int)gridDim.x / S_split : (int)gridDim.x;
-    const int k0 = a.nk * rank / S_split, k1 = a.nk * (rank + 1) / S_split;
-    const int nks = k1 - k0;
-    const int my_tiles = a.n_tiles > tile_base ? (a.n_tiles - 1 - tile_base) / tile_stride + 1 : 0;
-    const int total_steps = my_tiles * nks;
-    const uint32_t a_bytes = (uint32_t)a.R * BK * 2;
-    const uint32_t x_bytes = (uint32_t)a.Bp * BK * 2;
     bool ok = true;
 
     if (warp == 0 && lane == 0) {
         // ---------------- producer
-        const CUtensorMap *maps[3] = {&tmA0, &tmA1, &tmA2};
-        const uint64_t stream_pol = policy_evict_first();  // weights are read once per step
-        // stage layout: [A sub-tiles 0..ksub-1][A1 sub-tiles (gate_up)][X sub-tiles 0..ksub-1]
-        auto stage_a = [&](int s, int i, int j) {
-            return smem + (size_t)s * a.stage_bytes + (size_t)(i * a.ksub + j) * a.a_tile_bytes;
-        };
-        auto stage_x = [&](int s, int j) {
-            return smem + (size_t)s * a.stage_bytes + (size_t)NA * a.ksub * a.a_tile_bytes + (size_t)j * x_bytes;
-        };
-        auto subs_of = [&](int ks) { return min(a.ksub, (a.K - ks * a.ksub * BK + BK - 1) / BK); };
-        auto issue_weights = [&](int it) {
-            const int s = it % S;
-            const int t = tile_base + (it / nks) * tile_stride;
-            const int ks = k0 + it % nks;
-            const int nsub = subs_of(ks);
-            int mat, row0;
-            tile_coords(a, t, mat, row0);
-            mbar_arrive_expect_tx(&full[s], nsub * (NA * a_bytes + x_bytes));
-            for (int j = 0; j < nsub; j++) {
-                const int col = (ks * a.ksub + j) * BK;
-                if (EPI == GATE_UP) {
-                    tma_load_2d_stream(stage_a(s, 0, j), &tmA0, col, row0, &full[s], stream_pol);
-                    tma_load_2d_stream(stage_a(s, 1, j), &tmA1, col, row0, &full[s], stream_pol);
-                } else {
-                    tma_load_2d_stream(stage_a(s, 0, j), maps[mat], col, row0, &full[s], stream_pol);
-                }
-            }
-        };
         auto issue_x = [&](int it) {
             const int ks = k0 + it % nks;
             const int nsub = subs_of(ks);
             for (int j = 0; j < nsub; j++) tma_load_2d(stage_x(it % S, j), &tmX, (ks * a.ksub + j) * BK, 0, &full[it % S]);
         };
-        const int pre = min(S, total_steps);
-        for (int it = 0; it < pre; it++) issue_weights(it);  // weights do not depend on the previous kernel
         pdl_wait();
         const bool res_load = EPI == RESIDUAL && a.res_tma && rank == 0 && my_tiles > 0;
         if (res_load) {  // x rows of this tile for every batch row: read by the epilogue
